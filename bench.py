@@ -1,0 +1,489 @@
+#!/usr/bin/env python
+"""Benchmark of the paged latent-cache decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                    [--mode exact|tc] [--impl ours|reference] [--with-wo]
+
+A step is one append + decode pass over the whole batch: one FP32 latent row
+per sequence is written into the FP16 cache through its block table (the
+same slot every step, so the attended length stays fixed), then the split-K
+decode (scores, mask, online softmax, latent context) and the log-sum-exp
+combine with the W_uv / W_v projection run; `--with-wo` adds the W_o output
+projection.  The default workload is the long-context one (8 sequences of
+131072 tokens, absorbed-MLA shapes: 128 heads, latent 512 + 64, block 64).
+
+Metric: achieved HBM TB/s = algorithmic bytes of the step / step time (the
+step time is reported as ms_per_step).  With N > 1 (torchrun) each sequence's
+blocks are split across the ranks and the per-rank (context, log-sum-exp)
+results are all-gathered over NCCL and merged; the time is the max over ranks.
+
+`--impl reference` times the reference's CPU implementation of the path (the
+C restatement of crates/plkv-core/src/lib.rs:941-1145 in oracle/, OpenMP over
+(sequence, head) on every host core) on a bounded sample of the same workload
+and reports the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PACKAGE = "latentpagedattention-rs_b200"
+METRIC = "paged latent decode µs/step and achieved HBM TB/s vs peak at 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+SPLIT_K_WORKLOADS = {"long_context"}      # sequences' blocks split across ranks
+BATCH_SHARD_WORKLOADS = {"mla_batch", "write_attend"}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="long_context")
+    ap.add_argument("--mode", default="auto", choices=["auto", "exact", "tc"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--with-wo", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="target CPU work of the bounded CPU-baseline sample")
+    return ap.parse_args()
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path, encoding="utf-8") as f:
+            return json.load(f), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    QUERY = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            cmd = ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                   "-lms", "100"]
+            if self.uuid:
+                cmd[1:1] = ["-i", self.uuid]
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path, encoding="utf-8") as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 10:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        busy = [v for v in sm if v > 0.5 * max(sm)] if sm else []
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[6:10]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(busy) if busy else None,
+                "sm_max_mhz": float(rows[0][3]) if rows[0][3].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- helpers
+
+def lpt_shard(lens: np.ndarray, world: int, rank: int) -> np.ndarray:
+    """Longest-processing-time assignment of sequences to ranks by tokens."""
+    order = np.argsort(-lens, kind="stable")
+    load = np.zeros(world, dtype=np.int64)
+    owner = np.zeros(len(lens), dtype=np.int64)
+    for b in order:
+        r = int(np.argmin(load))
+        owner[b] = r
+        load[r] += int(lens[b])
+    return np.nonzero(owner == rank)[0]
+
+
+def cpu_sample_rate(s, x_host: dict, seconds: float, threads: int) -> dict:
+    """Time the reference CPU path (C restatement, OpenMP) on a bounded sample.
+
+    The sample is sequence 0 with the first `heads` query heads (and their
+    projection heads), grown until one run takes about `seconds`.  Returns
+    the extrapolated time of the full step.
+    """
+    from oracle import c_ref
+
+    c_ref.build()
+    n0 = int(x_host["lens"][0])
+    group = s.group
+    heads = max(group, min(s.q_heads, threads * group))
+    heads -= heads % group
+    while True:
+        ph = heads // group
+        q_lat = x_host["q_lat"][:1, :heads]
+        w = np.ascontiguousarray(x_host["w_v_hm"][:ph].transpose(1, 0, 2).reshape(s.value_dim, -1))
+        t0 = time.perf_counter()
+        c_ref.latent_decode_batch(q_lat, x_host["cache_bits"], x_host["tables"][:1],
+                                  x_host["lens"][:1], s.block_size, s.scale, s.value_dim, w, ph,
+                                  s.head_dim, threads=threads)
+        dt = time.perf_counter() - t0
+        if dt >= 0.25 * seconds or heads >= s.q_heads:
+            break
+        heads = min(s.q_heads, heads * 2)
+    work_sample = n0 * heads
+    work_full = int(np.sum(x_host["global_lens"].astype(np.int64))) * s.q_heads
+    return {"seconds": dt, "full_seconds": dt * work_full / work_sample,
+            "sample": f"sequence 0 ({n0} tokens) x {heads} of {s.q_heads} query heads, "
+                      f"extrapolated by tokens x heads to the full step", "threads": threads}
+
+
+def host_sample_inputs(s, x: dict, dev_tensors: bool = True) -> dict:
+    """Host copies of what the CPU sample reads (sequence 0 only)."""
+    import torch
+
+    tables = x["tables"].cpu().numpy()
+    nb = int((x["global_lens"][0] + s.block_size - 1) // s.block_size)
+    used = tables[0, :nb]
+    # Compact sequence 0's blocks into a small host pool.
+    cache = x["cache"][torch.as_tensor(used, device=x["cache"].device)].contiguous()
+    bits = cache.view(torch.int16).cpu().numpy().view(np.uint16)
+    local_table = np.arange(nb, dtype=np.int32)[None]
+    if "q_lat" in x:
+        q_lat = x["q_lat"][:1].cpu().numpy()
+    else:
+        from oracle import c_ref
+
+        wk = x["w_k"].cpu().numpy()
+        canon = wk.transpose(1, 0, 2).reshape(wk.shape[1], -1)
+        q_lat = c_ref.project_query(x["q"][0].cpu().numpy(), canon, s.kv_heads)[None]
+    return {"cache_bits": bits, "tables": local_table, "lens": x["global_lens"][:1].astype(np.int32),
+            "global_lens": x["global_lens"], "q_lat": q_lat,
+            "w_v_hm": x["w_v"].cpu().numpy()}
+
+
+# -------------------------------------------------------------- reference arm
+
+def run_reference(args, s, rank: int, world: int):
+    if rank != 0:
+        return
+    import torch
+
+    dev = torch.device("cuda:0") if torch.cuda.is_available() else torch.device("cpu")
+    from oracle import c_ref
+
+    threads = c_ref.max_threads()
+    # Inputs of sequence 0 are generated exactly as our arm does (device
+    # generator), then copied to the host for the CPU path.
+    wl = importlib.import_module(PACKAGE + ".workloads")
+    x = wl.device_inputs(s, dev, with_out_proj=False)
+    xh = host_sample_inputs(s, x)
+    del x
+    torch.cuda.empty_cache()
+    per_step = []
+    r = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_sample_rate(s, xh, args.cpu_seconds / max(1, args.steps), threads)
+        if i >= args.warmup:
+            per_step.append(r["full_seconds"])
+    t = statistics.median(per_step)
+    lens = wl.initial_lens(s)
+    algo = wl.algorithmic_bytes(s, lens, with_out_proj=args.with_wo)
+    value = algo / t / 1e12
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t * 1e3, "us_per_step": t * 1e6, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": s.name, "batch": s.batch, "q_heads": s.q_heads,
+                       "latent_dim": s.latent_dim, "value_dim": s.value_dim,
+                       "block_size": s.block_size, "tokens": int(lens.sum()),
+                       "w_o": bool(args.with_wo and s.out_dim)},
+            "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads,
+                             "kind": "port", "sample": r["sample"]},
+            "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+
+def run_ours(args, s, rank: int, world: int):
+    import torch
+    import torch.distributed as dist
+
+    ops = importlib.import_module(PACKAGE + ".ops")
+    wl = importlib.import_module(PACKAGE + ".workloads")
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    mode = args.mode
+    if mode == "auto":
+        mode = "tc" if (s.absorbed and ops.tc_available(s)) else "exact"
+    split_k = world > 1 and s.name in SPLIT_K_WORKLOADS
+    x = wl.device_inputs(s, dev, shards=world if split_k else 1, shard=rank if split_k else 0,
+                         with_out_proj=args.with_wo)
+    global_lens = x["global_lens"]
+    B = s.batch
+    seqs = np.arange(B)
+    if world > 1 and not split_k:
+        seqs = lpt_shard(global_lens, world, rank) if s.name in BATCH_SHARD_WORKLOADS else seqs
+    sel = torch.as_tensor(seqs, device=dev)
+    tables = x["tables"][sel].contiguous()
+    lens_host = np.asarray(x["lens"])[seqs].astype(np.int32)
+    lens = torch.as_tensor(lens_host, device=dev)
+    nb_local = len(seqs)
+    q_in = (x["q_lat"] if s.absorbed else x["q"])[sel].contiguous()
+    new_rows = x["new_rows"][sel].contiguous()
+    # The appended row lands on the last token (same slot every step).
+    gpos = global_lens[seqs].astype(np.int64) - 1
+    if split_k:
+        tb = x["tables"].cpu().numpy()
+        first = (((global_lens.astype(np.int64) + s.block_size - 1) // s.block_size) * rank) // world
+        slots = np.full(nb_local, -1, dtype=np.int64)
+        for i, b in enumerate(seqs):
+            lb = gpos[i] // s.block_size - first[b]
+            if 0 <= lb < tb.shape[1] and tb[b, lb] >= 0:
+                slots[i] = int(tb[b, lb]) * s.block_size + int(gpos[i] % s.block_size)
+        slots_d = torch.as_tensor(slots, device=dev)
+        positions = None
+    else:
+        positions = torch.as_tensor((gpos).astype(np.int32), device=dev)
+    plan = ops.plan_splits(lens_host, s.block_size, device=dev)
+    D = s.head_dim
+    ctx = torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
+    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, nb_local, s.q_heads, s.value_dim),
+                     dtype=torch.uint8, device=dev)
+    want_lse = split_k
+    gathered_ctx = torch.empty((world, nb_local, s.q_heads, D), dtype=torch.float32,
+                               device=dev) if split_k else None
+    gathered_lse = torch.empty((world, nb_local, s.q_heads), dtype=torch.float32,
+                               device=dev) if split_k else None
+    w_o = x.get("w_o")
+    out = (torch.empty((nb_local, s.out_dim), dtype=torch.float32, device=dev)
+           if w_o is not None else None)
+    wo_ws = None
+
+    def step(q_src, rows_src, ev=None):
+        nonlocal wo_ws
+        if split_k:
+            ops.latent_append_slots(rows_src, x["cache"], slots_d)
+        else:
+            ops.latent_append(rows_src, x["cache"], tables, positions=positions)
+        q_lat = q_src if s.absorbed else ops.project_query(q_src, x["w_k"])
+        if ev is not None:
+            ev[0].record()
+        r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
+                              value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
+                              want_lse=want_lse, workspace=ws, allow_empty=split_k,
+                              phase="partial")
+        if ev is not None:
+            ev[1].record()
+        r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
+                              value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
+                              want_lse=want_lse, workspace=ws, allow_empty=split_k,
+                              phase="combine")
+        res = ctx
+        if split_k:
+            dist.all_gather_into_tensor(gathered_ctx, ctx)
+            dist.all_gather_into_tensor(gathered_lse, r["lse"])
+            res, _ = ops.lse_merge(gathered_ctx, gathered_lse)
+        if w_o is not None:
+            if wo_ws is None:
+                wo_ws = torch.empty(1, dtype=torch.uint8, device=dev)
+            o = ops.out_proj(res.reshape(nb_local, -1), w_o, out=out)
+            res = o
+        return res
+
+    launches_per_step = 3 + (0 if s.absorbed else 1) + (1 if split_k else 0) + \
+        (2 if w_o is not None else 0)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step(q_in, new_rows)
+    barrier()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        uuid = None
+    clocks = ClockSampler(uuid) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    start.record()
+    for i in range(args.steps):
+        step(q_in, new_rows, kev[i])
+    end.record()
+    barrier()
+    elapsed_ms = start.elapsed_time(end)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    clock_info = clocks.stop() if clocks else None
+    t = torch.tensor([elapsed_ms, kern_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, kern_ms = float(t[0]), float(t[1])
+    ms_per_step = elapsed_ms / args.steps
+
+    # End to end through the public API with host buffers: H2D of the step's
+    # query and new rows, the step, D2H of the result.
+    e2e = None
+    if not args.no_e2e:
+        q_host = q_in.cpu().pin_memory()
+        rows_host = new_rows.cpu().pin_memory()
+        q_dev = torch.empty_like(q_in)
+        rows_dev = torch.empty_like(new_rows)
+        res_shape = (nb_local, s.out_dim) if w_o is not None else (nb_local, s.q_heads, D)
+        res_host = torch.empty(res_shape, dtype=torch.float32).pin_memory()
+        for _ in range(2):
+            q_dev.copy_(q_host, non_blocking=True)
+            rows_dev.copy_(rows_host, non_blocking=True)
+            res_host.copy_(step(q_dev, rows_dev), non_blocking=True)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        n_e2e = max(3, args.steps // 2)
+        e0.record()
+        for _ in range(n_e2e):
+            q_dev.copy_(q_host, non_blocking=True)
+            rows_dev.copy_(rows_host, non_blocking=True)
+            res_host.copy_(step(q_dev, rows_dev), non_blocking=True)
+        e1.record()
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1) / n_e2e], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te[0])
+        h2d = q_host.numel() * 4 + rows_host.numel() * 4
+        d2h = res_host.numel() * 4
+        if world > 1:
+            hb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
+            dist.all_reduce(hb)
+            h2d, d2h = int(hb[0]), int(hb[1])
+        e2e = {"ms_per_step": e2e_ms, "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h)}
+
+    if rank != 0:
+        return None
+    peaks, peak_kind = load_peaks()
+    algo = wl.algorithmic_bytes(s, global_lens, with_out_proj=w_o is not None)
+    value = algo / (ms_per_step * 1e-3) / 1e12
+    # Roofline of the dominant kernel (split-K partial pass on rank 0):
+    # latent rows attended x L x 2 bytes + query + table entries, per launch.
+    toks_local = int(np.sum(lens_host, dtype=np.int64))
+    kern_bytes = (toks_local * s.latent_dim * 2 + nb_local * s.q_heads * s.latent_dim * 4
+                  + int(np.sum((lens_host.astype(np.int64) + s.block_size - 1)
+                               // s.block_size)) * 4)
+    hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "traffic": None, "kernel": f"latent partial ({mode})",
+                "kernel_ms": kern_ms, "bytes_per_launch": kern_bytes,
+                "peak_source": f"{peak_kind} hbm_gbs"}
+    flops = wl.algorithmic_flops(s, lens_host, with_out_proj=False)
+    roofline["achieved_tflops"] = flops / (kern_ms * 1e-3) / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "us_per_step": ms_per_step * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32" if mode == "exact" else "f16",
+            "data": "synthetic (seeded, device-generated)",
+            "config": {"workload": s.name, "mode": mode, "batch": s.batch,
+                       "q_heads": s.q_heads, "latent_dim": s.latent_dim,
+                       "value_dim": s.value_dim, "head_dim": D, "block_size": s.block_size,
+                       "tokens": int(global_lens.sum()), "w_o": w_o is not None,
+                       "parallelism": (f"split-k{world}" if split_k else
+                                       (f"dp{world}" if world > 1 else "single")),
+                       "l2": "inputs larger than L2 (no flush)" if algo > 126e6
+                             else "inputs smaller than L2",
+                       "work_items": plan.n_items},
+            "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
+            "clocks": clock_info}
+    if e2e:
+        line["e2e"] = {"value": algo / (e2e["ms_per_step"] * 1e-3) / 1e12, "unit": "TB/s",
+                       "ms_per_step": e2e["ms_per_step"],
+                       "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
+                       "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]}
+    if world == 1 and not args.no_cpu_baseline:
+        from oracle import c_ref
+
+        xh = host_sample_inputs(s, x)
+        r = cpu_sample_rate(s, xh, args.cpu_seconds, c_ref.max_threads())
+        line["cpu_baseline"] = {"value": algo / r["full_seconds"] / 1e12, "unit": "TB/s",
+                                "cores": r["threads"], "kind": "port", "sample": r["sample"],
+                                "full_step_seconds_extrapolated": r["full_seconds"]}
+    return line
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    wl = importlib.import_module(PACKAGE + ".workloads")
+    s = wl.spec(args.workload)
+    if args.impl == "reference":
+        run_reference(args, s, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    if world > 1:
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    try:
+        line = run_ours(args, s, rank, world)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

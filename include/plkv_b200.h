@@ -1,0 +1,251 @@
+/*
+ * plkv_b200.h -- C ABI of the B200 (sm_100a) paged latent-cache decode library
+ * (libplkv_b200.so).
+ *
+ * Drop-in boundary for the hot path of tatavishnurao/LatentPagedAttention-rs:
+ * the FP32 -> FP16 latent-row write through a block table, the direct
+ * latent-space decode (scores, active-length mask, stable softmax, latent
+ * context, W_v / W_uv projection), the W_o output projection and the FP16
+ * full-KV paged GQA baseline.  The reference has no FFI of its own; each entry
+ * point cites the reference function (Python oracle and Rust CPU reference)
+ * whose argument meaning and error behaviour it keeps.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer to caller-owned memory unless the name
+ *     ends in `_host`.  The library allocates no device memory.
+ *   - Every launch is stream-ordered on `stream` (a cudaStream_t); no call
+ *     synchronises.  Calls are thread-safe.
+ *   - Return values are plkv_status codes.  Host-detectable argument errors
+ *     return before anything is launched.  Data-dependent errors found on the
+ *     device (a non-finite row, a table entry outside the pool) never trap:
+ *     the row / block is skipped and a PLKV_FLAG_* bit is OR-ed into the
+ *     caller's int32 `err_flags` word (may be NULL), which the caller reads
+ *     after the stream work completes.
+ *   - FP16 cache data is passed as uint16_t bit patterns (IEEE binary16).
+ *   - Offsets into pools are 64-bit; block ids and lengths are int32.
+ */
+#ifndef PLKV_B200_H
+#define PLKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* plkv_stream_t; /* same type as cudaStream_t */
+
+/* Status codes.  1-5 mirror PlkvError (crates/plkv-core/src/lib.rs:12-18). */
+enum plkv_status {
+    PLKV_OK = 0,
+    PLKV_ERR_ZERO_VALUE = 1,           /* PlkvError::ZeroValue            lib.rs:13 */
+    PLKV_ERR_ARITHMETIC_OVERFLOW = 2,  /* PlkvError::ArithmeticOverflow   lib.rs:14 */
+    PLKV_ERR_INVALID_PAGED_LOOKUP = 3, /* PlkvError::InvalidPagedLookup   lib.rs:15 */
+    PLKV_ERR_TOKEN_OUT_OF_RANGE = 4,   /* PlkvError::TokenOutOfRange      lib.rs:16 */
+    PLKV_ERR_TOKEN_NOT_ALLOCATED = 5,  /* PlkvError::TokenNotAllocated    lib.rs:17 */
+    PLKV_ERR_NON_FINITE = 6,           /* "FP16 storage input must be finite" lib.rs:307-311 */
+    PLKV_ERR_FP16_OVERFLOW = 7,        /* "FP16 storage conversion overflowed" lib.rs:313-316 */
+    PLKV_ERR_INVALID_ARGUMENT = 8,     /* null pointer / unsupported shape */
+    PLKV_ERR_WORKSPACE = 9,            /* workspace too small */
+    PLKV_ERR_CUDA = 10,                /* a CUDA runtime call failed */
+    PLKV_ERR_UNSUPPORTED = 11,         /* mode / shape not built for this device */
+};
+
+/* Device-side error flags (OR-ed into *err_flags). */
+#define PLKV_FLAG_NON_FINITE_INPUT 0x1 /* row rejected: NaN/Inf input          lib.rs:307-311 */
+#define PLKV_FLAG_FP16_OVERFLOW 0x2    /* row rejected: |x| rounds to inf      lib.rs:313-316 */
+#define PLKV_FLAG_BAD_BLOCK 0x4        /* table entry outside [0, num_physical) lib.rs:178-182 */
+#define PLKV_FLAG_BAD_POSITION 0x8     /* position not covered by the table    lib.rs:171-176 */
+#define PLKV_FLAG_BAD_LENGTH 0x10      /* seq_len outside [0, max_blocks*bs]   lib.rs:1106-1111 */
+
+/* Decode arithmetic. */
+#define PLKV_MODE_EXACT_F32 0 /* FP32 CUDA cores: parity mode, 1e-5 relative */
+#define PLKV_MODE_TC_F16 1    /* tcgen05 FP16 operands, FP32 TMEM accumulation (~2e-3) */
+
+const char* plkv_status_string(int status);
+int plkv_version(void);
+
+/* ------------------------------------------------------------------ storage */
+
+/* FP32 -> FP16 storage bits, round to nearest even.
+ * Replaces quantize_f32_to_f16_storage (crates/plkv-core/src/lib.rs:302-319)
+ * and fp16_storage_bits (python_ref/latent_paged_attention/cache_ref.py:17-19).
+ * Non-finite inputs set PLKV_FLAG_NON_FINITE_INPUT, overflow sets
+ * PLKV_FLAG_FP16_OVERFLOW (the output element is still written). */
+int plkv_quantize_f16(const float* in, uint16_t* out, int64_t n, int32_t* err_flags,
+                      plkv_stream_t stream);
+
+/* Writes one FP32 latent row per request into the FP16 latent cache
+ * cache[num_physical, block_size, latent_dim] at the slot of `positions[i]`
+ * through the block table of sequence `seq_ids[i]` (seq_ids NULL: i).
+ * Replaces paged_latent_write_fp16_storage (lib.rs:889-939) and
+ * paged_latent_write_fp16_storage_ref (cache_ref.py:103-114), batched and in
+ * place.  A row with any non-finite / overflowing element is not written at
+ * all (the reference rejects the whole write).
+ * If `seq_lens_inout` is not NULL, positions are taken from it (positions may
+ * be NULL) and each successful write increments it: an append. */
+int plkv_latent_append_f16(const float* rows, const int32_t* block_tables, int64_t max_blocks,
+                           const int32_t* seq_ids, const int32_t* positions,
+                           int32_t* seq_lens_inout, int64_t n_rows, uint16_t* cache,
+                           int64_t num_physical, int32_t block_size, int32_t latent_dim,
+                           int32_t* err_flags, plkv_stream_t stream);
+
+/* Slot-mapped form of the append: slot = physical_block * block_size + offset
+ * (negative slots are padding and are skipped).  Same per-row rules. */
+int plkv_latent_append_slots_f16(const float* rows, const int64_t* slots, int64_t n_rows,
+                                 uint16_t* cache, int64_t num_slots, int32_t latent_dim,
+                                 int32_t* err_flags, plkv_stream_t stream);
+
+/* Writes one K row and one V row ([kv_heads, head_dim] FP32 each) per request
+ * into FP16 head-major caches [num_physical, kv_heads, block_size, head_dim]
+ * (the layout of lib.rs:1232).  Replaces paged_kv_write_f32 (lib.rs:190-247)
+ * and paged_kv_write_ref (cache_ref.py:43-73) for the FP16 full-KV baseline. */
+int plkv_kv_append_f16(const float* k_rows, const float* v_rows, const int32_t* block_tables,
+                       int64_t max_blocks, const int32_t* seq_ids, const int32_t* positions,
+                       int32_t* seq_lens_inout, int64_t n_rows, uint16_t* k_cache,
+                       uint16_t* v_cache, int64_t num_physical, int32_t kv_heads,
+                       int32_t block_size, int32_t head_dim, int32_t* err_flags,
+                       plkv_stream_t stream);
+
+/* ---------------------------------------------------------------- planning */
+
+/* One unit of split-K work: tokens [block_begin*bs, min(block_end*bs, len))
+ * of sequence `seq`. */
+typedef struct plkv_work_item {
+    int32_t seq;
+    int32_t block_begin;
+    int32_t block_end;
+    int32_t reserved;
+} plkv_work_item;
+
+/* Host-side split planner (no CUDA calls).  Cuts every sequence's blocks into
+ * contiguous items of near-equal size so that about `target_items` items
+ * cover the batch, none shorter than `min_blocks` blocks.  Items are ordered
+ * by sequence; seq_item_begin_host[b]..[b+1] are sequence b's items.  A
+ * sequence of length 0 gets one empty item.  Returns PLKV_ERR_WORKSPACE if
+ * `max_items` is too small (n_items_host then holds the count needed). */
+int plkv_plan_splits(const int32_t* seq_lens_host, int32_t batch, int32_t block_size,
+                     int32_t target_items, int32_t min_blocks, plkv_work_item* items_host,
+                     int32_t max_items, int32_t* seq_item_begin_host, int32_t* n_items_host);
+
+/* ------------------------------------------------------------------ decode */
+
+/* Query projection q_lat[b, h, :] = W_k[kv(h)] q[b, h, :] with W_k head-major
+ * [kv_heads, latent_dim, head_dim], kv(h) = h / (q_heads / kv_heads).
+ * Replaces the `projected` loop of lib.rs:1026-1032 / attention_ref.py:513. */
+int plkv_project_query(const float* q, const float* w_k, float* q_lat, int32_t batch,
+                       int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t latent_dim,
+                       plkv_stream_t stream);
+
+/* Arguments of the direct paged latent decode. */
+typedef struct plkv_latent_decode_args {
+    const float* q_lat;           /* [batch, q_heads, latent_dim] projected / absorbed query */
+    const uint16_t* cache;        /* [num_physical, block_size, latent_dim] FP16 */
+    int64_t num_physical;
+    int32_t block_size;
+    int32_t latent_dim;           /* row width used by the scores (e.g. 576) */
+    int32_t value_dim;            /* leading columns used by the context (e.g. 512) */
+    int32_t batch;
+    int32_t q_heads;
+    float scale;                  /* 1/sqrt(head_dim) in the reference (lib.rs:1023) */
+    const int32_t* block_tables;  /* [batch, max_blocks] physical block ids */
+    int64_t max_blocks;
+    const int32_t* seq_lens;      /* [batch] active lengths */
+    const plkv_work_item* items;  /* [n_items] from plkv_plan_splits, on the device */
+    const int32_t* seq_item_begin;/* [batch + 1] on the device */
+    int32_t n_items;
+    int32_t allow_empty;          /* 1: a sequence of length 0 yields ctx 0, lse -inf */
+    const float* w_v;             /* [proj_heads, value_dim, head_dim] or NULL (latent ctx out) */
+    int32_t proj_heads;
+    int32_t head_dim;
+    float* ctx;                   /* [batch, q_heads, head_dim] (value_dim if w_v == NULL) */
+    float* lse;                   /* optional [batch, q_heads]: max + log(sum) of the scores */
+    float* scores;                /* optional [batch, q_heads, max_seq_len]; masked = -FLT_MAX */
+    float* probs;                 /* optional [batch, q_heads, max_seq_len]; masked = 0 */
+    int32_t max_seq_len;
+    int32_t mode;                 /* PLKV_MODE_* */
+    void* workspace;
+    size_t workspace_bytes;
+    int32_t* err_flags;           /* optional */
+} plkv_latent_decode_args;
+
+/* Workspace bytes the decode needs for `n_items` items. */
+size_t plkv_latent_decode_workspace_size(int32_t n_items, int32_t batch, int32_t q_heads,
+                                         int32_t value_dim);
+
+/* Direct paged latent decode: split-K partial pass over the work items
+ * (scores, active-length mask, online softmax, latent context), then the
+ * log-sum-exp combine fused with the W_v / W_uv projection.
+ * Replaces direct_paged_latent_gqa_decode_fp16_storage_runtime_f32_accum
+ * (lib.rs:1090-1145, core at 941-1088) and
+ * direct_paged_latent_gqa_fp16_storage_runtime_intermediates_ref
+ * (attention_ref.py:617-648), batched with a table and a length per sequence.
+ * Inactive positions come out as score -3.4028234663852886e38 and
+ * probability 0 (lib.rs:1130-1140, attention_ref.py:604-609). */
+int plkv_latent_decode(const plkv_latent_decode_args* args, plkv_stream_t stream);
+
+/* The two halves of plkv_latent_decode, for callers that schedule them. */
+int plkv_latent_decode_partial(const plkv_latent_decode_args* args, plkv_stream_t stream);
+int plkv_latent_decode_combine(const plkv_latent_decode_args* args, plkv_stream_t stream);
+
+/* Log-sum-exp merge of per-shard results (split-K across GPUs):
+ * ctx_shards [n_shards, rows, width] are normalised partial contexts and
+ * lse_shards [n_shards, rows] their log-sum-exp (-inf = empty shard).
+ * out[rows, width] = sum_s exp(lse_s - M) ctx_s / sum_s exp(lse_s - M). */
+int plkv_lse_merge(const float* ctx_shards, const float* lse_shards, int32_t n_shards,
+                   int64_t rows, int32_t width, float* out, float* lse_out,
+                   plkv_stream_t stream);
+
+/* W_o output projection out[batch, out_dim] = x[batch, in_dim] W_o[in_dim, out_dim]
+ * (FP32; extension -- the reference stops at the per-head context).
+ * The workspace holds k_splits * batch * out_dim floats. */
+size_t plkv_out_proj_workspace_size(int32_t batch, int32_t out_dim, int32_t k_splits);
+int plkv_out_proj(const float* x, const float* w_o, float* out, int32_t batch, int32_t in_dim,
+                  int32_t out_dim, int32_t k_splits, void* workspace, size_t workspace_bytes,
+                  plkv_stream_t stream);
+
+/* ------------------------------------------------------ full-KV baseline */
+
+typedef struct plkv_fullkv_decode_args {
+    const float* q;               /* [batch, q_heads, head_dim] */
+    const uint16_t* k_cache;      /* [num_physical, kv_heads, block_size, head_dim] FP16 */
+    const uint16_t* v_cache;
+    int64_t num_physical;
+    int32_t kv_heads;
+    int32_t block_size;
+    int32_t head_dim;
+    int32_t batch;
+    int32_t q_heads;
+    float scale;
+    const int32_t* block_tables;
+    int64_t max_blocks;
+    const int32_t* seq_lens;
+    const plkv_work_item* items;
+    const int32_t* seq_item_begin;
+    int32_t n_items;
+    int32_t allow_empty;
+    float* ctx;                   /* [batch, q_heads, head_dim] */
+    float* lse;
+    float* scores;
+    float* probs;
+    int32_t max_seq_len;
+    void* workspace;
+    size_t workspace_bytes;
+    int32_t* err_flags;
+} plkv_fullkv_decode_args;
+
+size_t plkv_fullkv_decode_workspace_size(int32_t n_items, int32_t batch, int32_t q_heads,
+                                         int32_t head_dim);
+
+/* FP16 full-KV paged GQA decode.  Replaces
+ * paged_full_kv_gqa_decode_fp16_storage_runtime_f32_accum (lib.rs:1147-1269)
+ * and paged_gqa_decode_attention_intermediates_ref (attention_ref.py:172-224)
+ * on FP16 storage, batched with a table and a length per sequence. */
+int plkv_fullkv_decode(const plkv_fullkv_decode_args* args, plkv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PLKV_B200_H */

@@ -1,0 +1,439 @@
+// plkv_decode_exact.cu -- FP32 CUDA-core ("exact" mode) decode kernels.
+//
+// Split-K partial pass of the direct paged latent decode (scores against the
+// projected query, active-length mask, online softmax, latent context) and of
+// the FP16 full-KV paged GQA baseline, plus the query projection.
+//
+// Arithmetic follows crates/plkv-core/src/lib.rs:1023-1071 (latent) and
+// lib.rs:1222-1263 (full KV): scores are an FP32 dot product over the latent
+// row in increasing column order, multiplied by `scale`; softmax uses expf of
+// (score - running max); contexts accumulate p * row in FP32.  The online
+// softmax keeps (max, sum, context) per work item; the combine pass merges
+// items exactly as the reference's single pass would up to FP32 rounding.
+#include "plkv_common.cuh"
+
+namespace plkv {
+
+// ---------------------------------------------------------------- latent
+
+// grid = (n_items, ceil(q_heads / 32)), block = 256 threads (8 warps).
+// Warp w owns heads 4w..4w+3 of the CTA's 32-head group in both phases:
+//   scores : lane = token of the 32-token tile, 4 dot products per thread;
+//   context: lane owns value columns 4*lane + 128*c (c < NCH), 4 heads.
+// Shared memory: q tile [32][L+4], row tile [32][L+4] (FP32, converted once
+// from FP16 when staged), probabilities [32 tokens][32 heads].
+template <int NCH>
+__global__ void __launch_bounds__(256, 1)
+latent_partial_exact_kernel(const float* __restrict__ q_lat, const uint16_t* __restrict__ cache,
+                            int64_t num_physical, int bs, int L, int Lv, int Hq, float scale,
+                            const int32_t* __restrict__ tables, int64_t max_blocks,
+                            const int32_t* __restrict__ seq_lens,
+                            const plkv_work_item* __restrict__ items, DecodeWorkspace ws,
+                            float* __restrict__ scores, int max_seq_len, int32_t* flags) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int LP = L + 4;
+    float* qs = reinterpret_cast<float*>(smem_raw);
+    float* lt = qs + kHeadGroup * LP;
+    float* ps = lt + kTileTokens * LP;
+    __shared__ const uint16_t* row_ptr[kTileTokens];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const plkv_work_item it = items[blockIdx.x];
+    const int b = it.seq;
+    const int h0 = blockIdx.y * kHeadGroup;
+    const int nh = min(kHeadGroup, Hq - h0);
+    int len = seq_lens[b];
+    const int64_t cap = max_blocks * (int64_t)bs;
+    if (len < 0 || len > cap) {
+        if (tid == 0 && blockIdx.y == 0) set_flag(flags, PLKV_FLAG_BAD_LENGTH);
+        len = len < 0 ? 0 : (int)cap;
+    }
+    const int t_begin = it.block_begin * bs;
+    const int t_end = min(it.block_end * bs, len);
+
+    for (int i = tid; i < kHeadGroup * L; i += 256) {
+        int h = i / L, k = i - h * L;
+        qs[h * LP + k] = (h < nh) ? q_lat[((int64_t)b * Hq + h0 + h) * L + k] : 0.f;
+    }
+
+    float m_run[4], l_run[4], acc[4][NCH][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        m_run[j] = -INFINITY;
+        l_run[j] = 0.f;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[j][c][e] = 0.f;
+    }
+
+    const int cpr = L >> 3;  // 16-byte chunks per row
+    for (int t0 = t_begin; t0 < t_end; t0 += kTileTokens) {
+        const int nt = min(kTileTokens, t_end - t0);
+        __syncthreads();  // previous tile consumed; q tile visible on the first pass
+        if (tid < kTileTokens) {
+            const uint16_t* rp = nullptr;
+            if (tid < nt) {
+                int t = t0 + tid;
+                int lb = t / bs;
+                int32_t phys = tables[(int64_t)b * max_blocks + lb];
+                if (phys >= 0 && phys < num_physical)
+                    rp = cache + ((int64_t)phys * bs + (t - lb * bs)) * (int64_t)L;
+                else
+                    set_flag(flags, PLKV_FLAG_BAD_BLOCK);
+            }
+            row_ptr[tid] = rp;
+        }
+        __syncthreads();
+        for (int i = tid; i < kTileTokens * cpr; i += 256) {
+            int r = i / cpr, c = i - r * cpr;
+            float v[8];
+            const uint16_t* rp = row_ptr[r];
+            if (rp) {
+                uint4 raw = __ldg(reinterpret_cast<const uint4*>(rp) + c);
+                unpack8(raw, v);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = 0.f;
+            }
+            float4* dst = reinterpret_cast<float4*>(lt + r * LP + c * 8);
+            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
+        __syncthreads();
+
+        // Scores: sequential FMA over the latent columns (lib.rs:1033-1041).
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* xr = lt + lane * LP;
+        const float* qw = qs + (4 * warp) * LP;
+#pragma unroll 4
+        for (int k = 0; k < L; k += 4) {
+            float4 x = *reinterpret_cast<const float4*>(xr + k);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float4 qv = *reinterpret_cast<const float4*>(qw + j * LP + k);
+                s[j] = fmaf(x.x, qv.x, s[j]);
+                s[j] = fmaf(x.y, qv.y, s[j]);
+                s[j] = fmaf(x.z, qv.z, s[j]);
+                s[j] = fmaf(x.w, qv.w, s[j]);
+            }
+        }
+        const bool tok_ok = lane < nt && row_ptr[lane] != nullptr;
+        float alpha[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int h = 4 * warp + j;
+            const float sc = s[j] * scale;
+            if (scores && lane < nt && h < nh && t0 + lane < max_seq_len)
+                scores[((int64_t)b * Hq + h0 + h) * max_seq_len + t0 + lane] = sc;
+            const float sv = tok_ok ? sc : -INFINITY;
+            const float m_new = fmaxf(m_run[j], warp_max(sv));
+            alpha[j] = (m_new == -INFINITY) ? 1.f : expf(m_run[j] - m_new);
+            const float p = tok_ok ? expf(sv - m_new) : 0.f;
+            l_run[j] = l_run[j] * alpha[j] + warp_sum(p);
+            m_run[j] = m_new;
+            ps[lane * kHeadGroup + 4 * warp + j] = p;
+        }
+        __syncwarp();
+
+        // Context: acc = acc * alpha + sum_r p[r] * row[r] (lib.rs:1057-1065).
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[j][c][e] *= alpha[j];
+        for (int r = 0; r < nt; ++r) {
+            const float4 pv = *reinterpret_cast<const float4*>(ps + r * kHeadGroup + 4 * warp);
+            const float* xr2 = lt + r * LP + lane * 4;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                if (lane * 4 + 128 * c < Lv) {
+                    const float4 x = *reinterpret_cast<const float4*>(xr2 + 128 * c);
+                    const float pj[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        acc[j][c][0] = fmaf(pj[j], x.x, acc[j][c][0]);
+                        acc[j][c][1] = fmaf(pj[j], x.y, acc[j][c][1]);
+                        acc[j][c][2] = fmaf(pj[j], x.z, acc[j][c][2]);
+                        acc[j][c][3] = fmaf(pj[j], x.w, acc[j][c][3]);
+                    }
+                }
+            }
+        }
+    }
+
+    const int64_t ib = blockIdx.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int h = 4 * warp + j;
+        if (h >= nh) continue;
+        const int64_t row = ib * Hq + h0 + h;
+        if (lane == 0) {
+            ws.part_m[row] = m_run[j];
+            ws.part_l[row] = l_run[j];
+        }
+        float* dst = ws.part_ctx + row * Lv;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            const int col = lane * 4 + 128 * c;
+            if (col < Lv)
+                *reinterpret_cast<float4*>(dst + col) =
+                    make_float4(acc[j][c][0], acc[j][c][1], acc[j][c][2], acc[j][c][3]);
+        }
+    }
+}
+
+size_t latent_exact_smem_bytes(int L) {
+    return size_t(kHeadGroup + kTileTokens) * (L + 4) * 4 + size_t(kTileTokens) * kHeadGroup * 4;
+}
+
+template <int NCH>
+static cudaError_t launch_latent_exact_t(const plkv_latent_decode_args& a, DecodeWorkspace ws,
+                                         cudaStream_t st) {
+    const size_t smem = latent_exact_smem_bytes(a.latent_dim);
+    cudaError_t e = cudaFuncSetAttribute(latent_partial_exact_kernel<NCH>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(a.n_items, (a.q_heads + kHeadGroup - 1) / kHeadGroup);
+    latent_partial_exact_kernel<NCH><<<grid, 256, smem, st>>>(
+        a.q_lat, a.cache, a.num_physical, a.block_size, a.latent_dim, a.value_dim, a.q_heads,
+        a.scale, a.block_tables, a.max_blocks, a.seq_lens, a.items, ws, a.scores, a.max_seq_len,
+        a.err_flags);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_latent_partial_exact(const plkv_latent_decode_args& a, DecodeWorkspace ws,
+                                        cudaStream_t st) {
+    const int nch = (a.value_dim + 127) / 128;
+    switch (nch) {
+        case 1: return launch_latent_exact_t<1>(a, ws, st);
+        case 2: return launch_latent_exact_t<2>(a, ws, st);
+        case 3: return launch_latent_exact_t<3>(a, ws, st);
+        case 4: return launch_latent_exact_t<4>(a, ws, st);
+        case 5: return launch_latent_exact_t<5>(a, ws, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// --------------------------------------------------------------- full KV
+
+// grid = (n_items, kv_heads), block = 256.  Warp w < G owns query head
+// kv*G + w; lane = token for the scores, lane owns columns 4*lane + 128*c of
+// the context.  K and V tiles of 32 tokens are staged in FP32.
+template <int NCH>
+__global__ void __launch_bounds__(256, 2)
+fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restrict__ k_cache,
+                            const uint16_t* __restrict__ v_cache, int64_t num_physical, int KV,
+                            int bs, int D, int Hq, float scale, const int32_t* __restrict__ tables,
+                            int64_t max_blocks, const int32_t* __restrict__ seq_lens,
+                            const plkv_work_item* __restrict__ items, DecodeWorkspace ws,
+                            float* __restrict__ scores, int max_seq_len, int32_t* flags) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int DP = D + 4;
+    const int G = Hq / KV;
+    float* qs = reinterpret_cast<float*>(smem_raw);  // [8][DP]
+    float* kt = qs + 8 * DP;                          // [32][DP]
+    float* vt = kt + kTileTokens * DP;                // [32][DP]
+    float* ps = vt + kTileTokens * DP;                // [32][8]
+    __shared__ int64_t row_off[kTileTokens];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const plkv_work_item it = items[blockIdx.x];
+    const int b = it.seq, g = blockIdx.y;
+    int len = seq_lens[b];
+    const int64_t cap = max_blocks * (int64_t)bs;
+    if (len < 0 || len > cap) {
+        if (tid == 0 && g == 0) set_flag(flags, PLKV_FLAG_BAD_LENGTH);
+        len = len < 0 ? 0 : (int)cap;
+    }
+    const int t_begin = it.block_begin * bs;
+    const int t_end = min(it.block_end * bs, len);
+    const bool active = warp < G;
+    const int h = g * G + warp;
+
+    for (int i = tid; i < 8 * D; i += 256) {
+        int w = i / D, d = i - w * D;
+        qs[w * DP + d] = (w < G) ? q[((int64_t)b * Hq + g * G + w) * D + d] : 0.f;
+    }
+    float m_run = -INFINITY, l_run = 0.f, acc[NCH][4];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
+
+    const int cpr = D >> 3;
+    for (int t0 = t_begin; t0 < t_end; t0 += kTileTokens) {
+        const int nt = min(kTileTokens, t_end - t0);
+        __syncthreads();
+        if (tid < kTileTokens) {
+            int64_t off = -1;
+            if (tid < nt) {
+                int t = t0 + tid;
+                int lb = t / bs;
+                int32_t phys = tables[(int64_t)b * max_blocks + lb];
+                if (phys >= 0 && phys < num_physical)
+                    off = (((int64_t)phys * KV + g) * bs + (t - lb * bs)) * (int64_t)D;
+                else
+                    set_flag(flags, PLKV_FLAG_BAD_BLOCK);
+            }
+            row_off[tid] = off;
+        }
+        __syncthreads();
+        for (int i = tid; i < 2 * kTileTokens * cpr; i += 256) {
+            const int which = i / (kTileTokens * cpr);
+            const int rem = i - which * kTileTokens * cpr;
+            const int r = rem / cpr, c = rem - r * cpr;
+            float v[8];
+            const int64_t off = row_off[r];
+            if (off >= 0) {
+                const uint16_t* base = which ? v_cache : k_cache;
+                uint4 raw = __ldg(reinterpret_cast<const uint4*>(base + off) + c);
+                unpack8(raw, v);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = 0.f;
+            }
+            float4* dst = reinterpret_cast<float4*>((which ? vt : kt) + r * DP + c * 8);
+            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
+        __syncthreads();
+        if (active) {
+            float s = 0.f;
+            const float* kr = kt + lane * DP;
+            const float* qr = qs + warp * DP;
+#pragma unroll 4
+            for (int d = 0; d < D; d += 4) {
+                float4 x = *reinterpret_cast<const float4*>(kr + d);
+                float4 qv = *reinterpret_cast<const float4*>(qr + d);
+                s = fmaf(qv.x, x.x, s);
+                s = fmaf(qv.y, x.y, s);
+                s = fmaf(qv.z, x.z, s);
+                s = fmaf(qv.w, x.w, s);
+            }
+            const float sc = s * scale;
+            const bool tok_ok = lane < nt && row_off[lane] >= 0;
+            if (scores && lane < nt && t0 + lane < max_seq_len)
+                scores[((int64_t)b * Hq + h) * max_seq_len + t0 + lane] = sc;
+            const float sv = tok_ok ? sc : -INFINITY;
+            const float m_new = fmaxf(m_run, warp_max(sv));
+            const float alpha = (m_new == -INFINITY) ? 1.f : expf(m_run - m_new);
+            const float p = tok_ok ? expf(sv - m_new) : 0.f;
+            l_run = l_run * alpha + warp_sum(p);
+            m_run = m_new;
+            ps[lane * 8 + warp] = p;
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[c][e] *= alpha;
+            for (int r = 0; r < nt; ++r) {
+                const float pr = ps[r * 8 + warp];
+                const float* vr = vt + r * DP + lane * 4;
+#pragma unroll
+                for (int c = 0; c < NCH; ++c) {
+                    if (lane * 4 + 128 * c < D) {
+                        const float4 x = *reinterpret_cast<const float4*>(vr + 128 * c);
+                        acc[c][0] = fmaf(pr, x.x, acc[c][0]);
+                        acc[c][1] = fmaf(pr, x.y, acc[c][1]);
+                        acc[c][2] = fmaf(pr, x.z, acc[c][2]);
+                        acc[c][3] = fmaf(pr, x.w, acc[c][3]);
+                    }
+                }
+            }
+        }
+    }
+    if (!active) return;
+    const int64_t row = (int64_t)blockIdx.x * Hq + h;
+    if (lane == 0) {
+        ws.part_m[row] = m_run;
+        ws.part_l[row] = l_run;
+    }
+    float* dst = ws.part_ctx + row * D;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int col = lane * 4 + 128 * c;
+        if (col < D)
+            *reinterpret_cast<float4*>(dst + col) =
+                make_float4(acc[c][0], acc[c][1], acc[c][2], acc[c][3]);
+    }
+}
+
+size_t fullkv_exact_smem_bytes(int D) {
+    return size_t(8 + 2 * kTileTokens) * (D + 4) * 4 + size_t(kTileTokens) * 8 * 4;
+}
+
+template <int NCH>
+static cudaError_t launch_fullkv_exact_t(const plkv_fullkv_decode_args& a, DecodeWorkspace ws,
+                                         cudaStream_t st) {
+    const size_t smem = fullkv_exact_smem_bytes(a.head_dim);
+    cudaError_t e = cudaFuncSetAttribute(fullkv_partial_exact_kernel<NCH>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(a.n_items, a.kv_heads);
+    fullkv_partial_exact_kernel<NCH><<<grid, 256, smem, st>>>(
+        a.q, a.k_cache, a.v_cache, a.num_physical, a.kv_heads, a.block_size, a.head_dim,
+        a.q_heads, a.scale, a.block_tables, a.max_blocks, a.seq_lens, a.items, ws, a.scores,
+        a.max_seq_len, a.err_flags);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fullkv_partial_exact(const plkv_fullkv_decode_args& a, DecodeWorkspace ws,
+                                        cudaStream_t st) {
+    switch ((a.head_dim + 127) / 128) {
+        case 1: return launch_fullkv_exact_t<1>(a, ws, st);
+        case 2: return launch_fullkv_exact_t<2>(a, ws, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// ------------------------------------------------------- query projection
+
+// grid = batch * kv_heads, block = 256.  q_lat[b, kv*G + j, l] =
+// sum_d W_k[kv, l, d] * q[b, kv*G + j, d]; warp per latent row, lanes over d.
+__global__ void __launch_bounds__(256)
+project_query_kernel(const float* __restrict__ q, const float* __restrict__ w_k,
+                     float* __restrict__ q_lat, int Hq, int KV, int D, int L) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float* qs = reinterpret_cast<float*>(smem_raw);  // [G][D]
+    const int G = Hq / KV;
+    const int b = blockIdx.x / KV, g = blockIdx.x % KV;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < G * D; i += 256) qs[i] = q[((int64_t)b * Hq + g * G) * D + i];
+    __syncthreads();
+    constexpr int kMaxPerLane = 8;  // D <= 256
+    for (int l = warp; l < L; l += 8) {
+        const float* wr = w_k + ((int64_t)g * L + l) * D;
+        float wv[kMaxPerLane];
+#pragma unroll
+        for (int i = 0; i < kMaxPerLane; ++i) {
+            int d = lane + 32 * i;
+            wv[i] = d < D ? wr[d] : 0.f;
+        }
+        for (int j = 0; j < G; ++j) {
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < kMaxPerLane; ++i) {
+                int d = lane + 32 * i;
+                if (d < D) acc = fmaf(wv[i], qs[j * D + d], acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) q_lat[((int64_t)b * Hq + g * G + j) * L + l] = acc;
+        }
+    }
+}
+
+cudaError_t launch_project_query(const float* q, const float* w_k, float* q_lat, int B, int Hq,
+                                 int KV, int D, int L, cudaStream_t st) {
+    const size_t smem = size_t(Hq / KV) * D * 4;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(project_query_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    project_query_kernel<<<B * KV, 256, smem, st>>>(q, w_k, q_lat, Hq, KV, D, L);
+    return cudaGetLastError();
+}
+
+}  // namespace plkv

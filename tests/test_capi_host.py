@@ -1,0 +1,133 @@
+"""C ABI of libplkv_b200.so without a GPU: every symbol of include/plkv_b200.h
+is exported and bound, host-side validation returns the reference's error
+codes before anything is launched, and the split planner's contract holds."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import PACKAGE, ROOT
+
+HEADER = os.path.join(ROOT, "include", "plkv_b200.h")
+
+
+def _lib_mod():
+    import importlib
+
+    return importlib.import_module(PACKAGE + "._lib")
+
+
+def header_functions() -> list[str]:
+    text = open(HEADER, encoding="utf-8").read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(plkv_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    m = _lib_mod()
+    lib = m.lib()
+    names = header_functions()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(m.SIGNATURES), "ctypes bindings must cover the header exactly"
+    assert lib.plkv_version() >= 100
+    assert lib.plkv_status_string(3) == b"invalid paged lookup"
+
+
+def test_status_codes_match_header():
+    m = _lib_mod()
+    text = open(HEADER, encoding="utf-8").read()
+    for name in ("ZERO_VALUE", "ARITHMETIC_OVERFLOW", "INVALID_PAGED_LOOKUP", "NON_FINITE",
+                 "FP16_OVERFLOW", "WORKSPACE", "UNSUPPORTED"):
+        v = int(re.search(rf"PLKV_ERR_{name} = (\d+)", text).group(1))
+        assert getattr(m, f"PLKV_ERR_{name}") == v
+
+
+def _plan(lens, bs, target, min_blocks=1):
+    m = _lib_mod()
+    lens = np.ascontiguousarray(np.asarray(lens, np.int32))
+    n = ctypes.c_int32(0)
+    st = m.lib().plkv_plan_splits(lens.ctypes.data, lens.size, bs, target, min_blocks, None, 0,
+                                  None, ctypes.byref(n))
+    assert st == m.PLKV_ERR_WORKSPACE
+    items = np.zeros((n.value, 4), np.int32)
+    begin = np.zeros(lens.size + 1, np.int32)
+    st = m.lib().plkv_plan_splits(lens.ctypes.data, lens.size, bs, target, min_blocks,
+                                  items.ctypes.data, n.value, begin.ctypes.data, ctypes.byref(n))
+    assert st == m.PLKV_OK
+    return items, begin
+
+
+@pytest.mark.parametrize("lens,bs,target", [
+    ([7, 13], 4, 296), ([256], 16, 296), ([131072] * 8, 64, 296), ([0, 5, 0], 4, 10),
+    (list(np.random.default_rng(3).integers(1024, 32769, 64)), 64, 296), ([1], 1, 1)])
+def test_plan_covers_every_block_once(lens, bs, target):
+    items, begin = _plan(lens, bs, target)
+    assert begin[0] == 0 and begin[-1] == len(items)
+    for b, n in enumerate(lens):
+        its = items[begin[b]:begin[b + 1]]
+        assert len(its) >= 1 and np.all(its[:, 0] == b)
+        nb = (n + bs - 1) // bs
+        covered = np.concatenate([np.arange(i[1], i[2]) for i in its]) if nb else np.array([])
+        np.testing.assert_array_equal(covered, np.arange(nb))
+    sizes = items[:, 2] - items[:, 1]
+    per = -(-sum((n + bs - 1) // bs for n in lens) // max(target, len(lens)))
+    assert sizes.max() <= max(per, 1)
+
+
+def test_plan_rejects_bad_arguments():
+    m = _lib_mod()
+    n = ctypes.c_int32(0)
+    lens = np.array([-1], np.int32)
+    assert m.lib().plkv_plan_splits(lens.ctypes.data, 1, 4, 4, 1, None, 0, None,
+                                    ctypes.byref(n)) == m.PLKV_ERR_INVALID_ARGUMENT
+    assert m.lib().plkv_plan_splits(lens.ctypes.data, 0, 4, 4, 1, None, 0, None,
+                                    ctypes.byref(n)) == m.PLKV_ERR_ZERO_VALUE
+
+
+def test_host_validation_before_launch():
+    """Argument errors return a status without touching the GPU."""
+    m = _lib_mod()
+    L = m.lib()
+    a = m.LatentDecodeArgs(batch=0, q_heads=4, latent_dim=8, value_dim=8, block_size=4,
+                           num_physical=6, max_blocks=4, n_items=1)
+    assert L.plkv_latent_decode(ctypes.byref(a), None) == m.PLKV_ERR_ZERO_VALUE
+    a.batch = 2
+    assert L.plkv_latent_decode(ctypes.byref(a), None) == m.PLKV_ERR_INVALID_ARGUMENT
+    fake = 256  # never dereferenced: validation fails first
+    a.q_lat = a.cache = a.block_tables = a.seq_lens = a.items = a.seq_item_begin = fake
+    a.ctx = a.workspace = fake
+    a.w_v, a.proj_heads, a.head_dim = fake, 3, 16   # 4 heads cannot map onto 3
+    assert L.plkv_latent_decode(ctypes.byref(a), None) == m.PLKV_ERR_INVALID_PAGED_LOOKUP
+    a.proj_heads = 2
+    a.latent_dim, a.value_dim = 12, 12               # rows must be 16-byte multiples
+    assert L.plkv_latent_decode(ctypes.byref(a), None) == m.PLKV_ERR_UNSUPPORTED
+    a.latent_dim, a.value_dim = 8, 8
+    a.workspace_bytes = 1
+    assert L.plkv_latent_decode(ctypes.byref(a), None) == m.PLKV_ERR_WORKSPACE
+    assert L.plkv_project_query(fake, fake, fake, 1, 6, 4, 16, 8, None) == \
+        m.PLKV_ERR_INVALID_PAGED_LOOKUP
+    assert L.plkv_latent_append_f16(fake, fake, 4, None, fake, None, 1, fake, 6, 0, 8, None,
+                                    None) == m.PLKV_ERR_ZERO_VALUE
+    assert L.plkv_latent_append_f16(fake, fake, 4, None, fake, None, 0, fake, 6, 4, 8, None,
+                                    None) == m.PLKV_OK
+    f = m.FullKVDecodeArgs(batch=1, q_heads=6, kv_heads=4, head_dim=16, block_size=4,
+                           num_physical=6, max_blocks=4, n_items=1)
+    assert L.plkv_fullkv_decode(ctypes.byref(f), None) == m.PLKV_ERR_INVALID_PAGED_LOOKUP
+    assert L.plkv_out_proj(fake, fake, fake, 65, 16, 16, 1, fake, 1 << 20, None) == \
+        m.PLKV_ERR_UNSUPPORTED
+    assert L.plkv_latent_decode_workspace_size(10, 2, 4, 8) > 10 * 4 * 8 * 4
+
+
+def test_product_never_imports_the_oracle():
+    pkg_dir = os.path.join(ROOT, PACKAGE)
+    for dirpath, _, files in os.walk(pkg_dir):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".h")):
+                text = open(os.path.join(dirpath, f), encoding="utf-8").read()
+                assert "import oracle" not in text and "from oracle" not in text, f
+                assert "plkv_oracle" not in text, f
