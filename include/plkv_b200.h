@@ -189,6 +189,24 @@ int plkv_latent_decode(const plkv_latent_decode_args* args, plkv_stream_t stream
 int plkv_latent_decode_partial(const plkv_latent_decode_args* args, plkv_stream_t stream);
 int plkv_latent_decode_combine(const plkv_latent_decode_args* args, plkv_stream_t stream);
 
+/* Size of the library's fixed scratch array used by plkv_latent_decode_noalloc. */
+#define PLKV_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* plkv_latent_decode for callers that cannot allocate device memory (a plugin
+ * host that owns every device byte and passes only inputs and outputs, or a
+ * binding with no CUDA allocator).  No counterpart in the reference.
+ * args->workspace / workspace_bytes are ignored: the split-K scratch is a
+ * file-scope device array of PLKV_NOALLOC_SCRATCH_BYTES that every GPU loading
+ * the library holds until exit.  Returns PLKV_ERR_WORKSPACE, launching
+ * nothing, when plkv_latent_decode_workspace_size(n_items, batch, q_heads,
+ * value_dim) exceeds that size (plan fewer work items).  Calls no cudaMalloc
+ * or cudaFree.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls share the array, so calls that overlap
+ * on the GPU race; it keeps the last call's contents, none of which a later
+ * call reads before writing. */
+int plkv_latent_decode_noalloc(const plkv_latent_decode_args* args, plkv_stream_t stream);
+
 /* Log-sum-exp merge of per-shard results (split-K across GPUs):
  * ctx_shards [n_shards, rows, width] are normalised partial contexts and
  * lse_shards [n_shards, rows] their log-sum-exp (-inf = empty shard).

@@ -84,6 +84,7 @@ SIGNATURES = {
     "plkv_latent_decode": (ctypes.c_int, [ctypes.POINTER(LatentDecodeArgs), _P]),
     "plkv_latent_decode_partial": (ctypes.c_int, [ctypes.POINTER(LatentDecodeArgs), _P]),
     "plkv_latent_decode_combine": (ctypes.c_int, [ctypes.POINTER(LatentDecodeArgs), _P]),
+    "plkv_latent_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(LatentDecodeArgs), _P]),
     "plkv_lse_merge": (ctypes.c_int, [_P, _P, _I32, _I64, _I32, _P, _P, _P]),
     "plkv_out_proj_workspace_size": (_SZ, [_I32, _I32, _I32]),
     "plkv_out_proj": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _I32, _P, _SZ, _P]),
