@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU work of the bounded CPU-baseline sample")
+    ap.add_argument("--seqs", type=int, default=0,
+                    help="keep only the first N sequences (small profiling cases)")
     return ap.parse_args()
 
 
@@ -466,6 +468,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     wl = importlib.import_module(PACKAGE + ".workloads")
     s = wl.spec(args.workload)
+    if args.seqs:
+        import dataclasses
+
+        s = dataclasses.replace(s, batch=args.seqs, lens=s.lens[:args.seqs])
     if args.impl == "reference":
         run_reference(args, s, rank, world)
         return

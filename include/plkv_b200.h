@@ -58,6 +58,7 @@ enum plkv_status {
 #define PLKV_FLAG_BAD_BLOCK 0x4        /* table entry outside [0, num_physical) lib.rs:178-182 */
 #define PLKV_FLAG_BAD_POSITION 0x8     /* position not covered by the table    lib.rs:171-176 */
 #define PLKV_FLAG_BAD_LENGTH 0x10      /* seq_len outside [0, max_blocks*bs]   lib.rs:1106-1111 */
+#define PLKV_FLAG_TIMEOUT 0x20         /* a tensor-core pipeline wait gave up (results invalid) */
 
 /* Decode arithmetic. */
 #define PLKV_MODE_EXACT_F32 0 /* FP32 CUDA cores: parity mode, 1e-5 relative */

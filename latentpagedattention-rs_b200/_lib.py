@@ -36,6 +36,7 @@ FLAG_FP16_OVERFLOW = 0x2
 FLAG_BAD_BLOCK = 0x4
 FLAG_BAD_POSITION = 0x8
 FLAG_BAD_LENGTH = 0x10
+FLAG_TIMEOUT = 0x20
 
 MODE_EXACT_F32 = 0
 MODE_TC_F16 = 1

@@ -205,6 +205,7 @@ static int validate_latent(const plkv_latent_decode_args* a) {
     if ((a->scores || a->probs) && a->max_seq_len <= 0) return PLKV_ERR_ZERO_VALUE;
     if (a->probs && !a->scores) return PLKV_ERR_INVALID_ARGUMENT;
     if (a->latent_dim % 8 || a->value_dim % 4 || a->value_dim > 640) return PLKV_ERR_UNSUPPORTED;
+    if (a->n_items > 65535) return PLKV_ERR_UNSUPPORTED;  // grid y of the partial pass
     if ((int64_t)a->max_blocks * a->block_size > 0x7fffffffLL) return PLKV_ERR_ARITHMETIC_OVERFLOW;
     if (a->workspace_bytes <
         decode_workspace_bytes(a->n_items, a->batch, a->q_heads, a->value_dim))

@@ -16,7 +16,9 @@ namespace plkv {
 
 // ---------------------------------------------------------------- latent
 
-// grid = (n_items, ceil(q_heads / 32)), block = 256 threads (8 warps).
+// grid = (ceil(q_heads / 32), n_items), block = 256 threads (8 warps); the
+// head groups of one work item are adjacent in launch order so that they read
+// the item's latent rows from L2 rather than each from HBM.
 // Warp w owns heads 4w..4w+3 of the CTA's 32-head group in both phases:
 //   scores : lane = token of the 32-token tile, 4 dot products per thread;
 //   context: lane owns value columns 4*lane + 128*c (c < NCH), 4 heads.
@@ -38,14 +40,14 @@ latent_partial_exact_kernel(const float* __restrict__ q_lat, const uint16_t* __r
     __shared__ const uint16_t* row_ptr[kTileTokens];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const plkv_work_item it = items[blockIdx.x];
+    const plkv_work_item it = items[blockIdx.y];
     const int b = it.seq;
-    const int h0 = blockIdx.y * kHeadGroup;
+    const int h0 = blockIdx.x * kHeadGroup;
     const int nh = min(kHeadGroup, Hq - h0);
     int len = seq_lens[b];
     const int64_t cap = max_blocks * (int64_t)bs;
     if (len < 0 || len > cap) {
-        if (tid == 0 && blockIdx.y == 0) set_flag(flags, PLKV_FLAG_BAD_LENGTH);
+        if (tid == 0 && blockIdx.x == 0) set_flag(flags, PLKV_FLAG_BAD_LENGTH);
         len = len < 0 ? 0 : (int)cap;
     }
     const int t_begin = it.block_begin * bs;
@@ -163,7 +165,7 @@ latent_partial_exact_kernel(const float* __restrict__ q_lat, const uint16_t* __r
         }
     }
 
-    const int64_t ib = blockIdx.x;
+    const int64_t ib = blockIdx.y;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int h = 4 * warp + j;
@@ -195,7 +197,7 @@ static cudaError_t launch_latent_exact_t(const plkv_latent_decode_args& a, Decod
     cudaError_t e = cudaFuncSetAttribute(latent_partial_exact_kernel<NCH>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid(a.n_items, (a.q_heads + kHeadGroup - 1) / kHeadGroup);
+    dim3 grid((a.q_heads + kHeadGroup - 1) / kHeadGroup, a.n_items);
     latent_partial_exact_kernel<NCH><<<grid, 256, smem, st>>>(
         a.q_lat, a.cache, a.num_physical, a.block_size, a.latent_dim, a.value_dim, a.q_heads,
         a.scale, a.block_tables, a.max_blocks, a.seq_lens, a.items, ws, a.scores, a.max_seq_len,

@@ -22,6 +22,7 @@ from tests_support import assert_close, model_shaped_inputs, regenerate, rel_err
 pytestmark = pytest.mark.gpu
 
 EXACT_REL = 1e-5
+TC_REL = 2e-3     # tensor-core mode: FP16 query and probabilities, FP32 accumulation
 DEV = "cuda"
 
 
@@ -321,7 +322,7 @@ def _mla_case(pkg, batch, lens, seed=5):
                 bs=bs, L=L, Lv=Lv, Hq=Hq, D=D, scale=1 / math.sqrt(D))
 
 
-def _check_mla(ops, m, mode, rel, heads=(0, 37, 127), target=None):
+def _check_mla(ops, m, mode, rel, heads=(0, 37, 127), target=None, lse_tol=1e-4):
     lens_host = m["lens"]
     plan = ops.plan_splits(lens_host, m["bs"], target_items=target)
     r = ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]), t(lens_host), plan,
@@ -342,7 +343,7 @@ def _check_mla(ops, m, mode, rel, heads=(0, 37, 127), target=None):
             srow = es[h, :n].astype(np.float64)
             mx = srow.max()
             e_lse = mx + math.log(np.exp(srow - mx).sum())
-            assert abs(lse[b, h] - e_lse) <= 1e-4 * max(1.0, abs(e_lse))
+            assert abs(lse[b, h] - e_lse) <= lse_tol * max(1.0, abs(e_lse))
     return r
 
 
@@ -350,6 +351,41 @@ def test_mla_exact_small_batch(ops, pkg):
     m = _mla_case(pkg, 3, [1, 777, 4096])
     _check_mla(ops, m, "exact", EXACT_REL)
     _check_mla(ops, m, "exact", EXACT_REL, target=1000)   # many splits, same answer
+
+
+@pytest.mark.parametrize("lens", [[1, 777, 4096], [64, 65, 3000], [32, 5000]])
+def test_mla_tensor_core_small_batch(ops, pkg, lens):
+    m = _mla_case(pkg, len(lens), lens, seed=7)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    plan = ops.plan_splits(m["lens"], m["bs"])
+    ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]), t(m["lens"]), plan,
+                      scale=m["scale"], value_dim=m["Lv"], w_v=t(m["w_uv"]), mode="tc",
+                      flags=flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
+    _check_mla(ops, m, "tc", TC_REL, heads=(0, 63, 64, 127), lse_tol=2e-3)
+    _check_mla(ops, m, "tc", TC_REL, heads=(5, 100), target=3, lse_tol=2e-3)
+
+
+def test_tensor_core_matches_exact_mode(ops, pkg):
+    m = _mla_case(pkg, 4, [900, 2048, 131, 6000], seed=13)
+    outs = {}
+    for mode in ("exact", "tc"):
+        plan = ops.plan_splits(m["lens"], m["bs"])
+        outs[mode] = ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]),
+                                       t(m["lens"]), plan, scale=m["scale"], value_dim=m["Lv"],
+                                       w_v=t(m["w_uv"]), mode=mode, want_lse=True)
+    assert rel_err(outs["tc"]["ctx"].cpu(), outs["exact"]["ctx"].cpu()) <= TC_REL
+    assert rel_err(outs["tc"]["lse"].cpu(), outs["exact"]["lse"].cpu()) <= TC_REL
+
+
+def test_tensor_core_rejects_intermediates(ops, pkg):
+    m = _mla_case(pkg, 1, [100], seed=3)
+    plan = ops.plan_splits(m["lens"], m["bs"])
+    with pytest.raises(Exception):
+        ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]), t(m["lens"]), plan,
+                          scale=m["scale"], value_dim=m["Lv"], w_v=t(m["w_uv"]), mode="tc",
+                          want_scores=True, max_seq_len=100)
 
 
 def test_split_invariance_and_empty_sequences(ops, pkg):
@@ -420,6 +456,20 @@ def test_long_context_full_size_sampled(ops, pkg):
                                               want_intermediates=False)
         assert rel_err(ctx[b, h], ec[h]) <= EXACT_REL, (b, h, rel_err(ctx[b, h], ec[h]))
     assert np.all(np.isfinite(ctx))
+
+
+def test_long_context_tensor_core_full_size(ops, pkg):
+    """Tensor-core mode on the full long-context workload against exact mode."""
+    s = pkg.workloads.spec("long_context")
+    x = pkg.workloads.device_inputs(s, DEV)
+    lens = t(x["lens"])
+    res = {}
+    for mode in ("exact", "tc"):
+        plan = ops.plan_splits(x["lens"], s.block_size)
+        res[mode] = ops.latent_decode(x["q_lat"], x["cache"], x["tables"], lens, plan,
+                                      scale=s.scale, value_dim=s.value_dim, w_v=x["w_v"],
+                                      mode=mode)["ctx"].cpu()
+    assert rel_err(res["tc"], res["exact"]) <= TC_REL
 
 
 def test_write_attend_fullkv_matches_latent(ops, pkg):
