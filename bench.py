@@ -133,18 +133,6 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- helpers
 
-def lpt_shard(lens: np.ndarray, world: int, rank: int) -> np.ndarray:
-    """Longest-processing-time assignment of sequences to ranks by tokens."""
-    order = np.argsort(-lens, kind="stable")
-    load = np.zeros(world, dtype=np.int64)
-    owner = np.zeros(len(lens), dtype=np.int64)
-    for b in order:
-        r = int(np.argmin(load))
-        owner[b] = r
-        load[r] += int(lens[b])
-    return np.nonzero(owner == rank)[0]
-
-
 def cpu_sample_rate(s, x_host: dict, seconds: float, threads: int) -> dict:
     """Time the reference CPU path (C restatement, OpenMP) on a bounded sample.
 
@@ -253,6 +241,7 @@ def run_ours(args, s, rank: int, world: int):
 
     ops = importlib.import_module(PACKAGE + ".ops")
     wl = importlib.import_module(PACKAGE + ".workloads")
+    mg = importlib.import_module(PACKAGE + ".multigpu")
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     mode = args.mode
@@ -264,8 +253,8 @@ def run_ours(args, s, rank: int, world: int):
     global_lens = x["global_lens"]
     B = s.batch
     seqs = np.arange(B)
-    if world > 1 and not split_k:
-        seqs = lpt_shard(global_lens, world, rank) if s.name in BATCH_SHARD_WORKLOADS else seqs
+    if world > 1 and not split_k and s.name in BATCH_SHARD_WORKLOADS:
+        seqs = np.nonzero(mg.lpt_assign(global_lens, world) == rank)[0]
     sel = torch.as_tensor(seqs, device=dev)
     tables = x["tables"][sel].contiguous()
     lens_host = np.asarray(x["lens"])[seqs].astype(np.int32)
@@ -276,21 +265,18 @@ def run_ours(args, s, rank: int, world: int):
     # The appended row lands on the last token (same slot every step).
     gpos = global_lens[seqs].astype(np.int64) - 1
     if split_k:
-        tb = x["tables"].cpu().numpy()
-        first = (((global_lens.astype(np.int64) + s.block_size - 1) // s.block_size) * rank) // world
-        slots = np.full(nb_local, -1, dtype=np.int64)
-        for i, b in enumerate(seqs):
-            lb = gpos[i] // s.block_size - first[b]
-            if 0 <= lb < tb.shape[1] and tb[b, lb] >= 0:
-                slots[i] = int(tb[b, lb]) * s.block_size + int(gpos[i] % s.block_size)
+        first, _, _ = mg.split_k_ranges(global_lens, s.block_size, world, rank, s.steps - 1)
+        slots = mg.append_slots(gpos, x["tables"].cpu().numpy(), first, s.block_size)
         slots_d = torch.as_tensor(slots, device=dev)
         positions = None
     else:
-        positions = torch.as_tensor((gpos).astype(np.int32), device=dev)
-    plan = ops.plan_splits(lens_host, s.block_size, device=dev)
+        positions = torch.as_tensor(gpos.astype(np.int32), device=dev)
+    plan = (ops.plan_workers(lens_host, s.block_size, device=dev) if mode == "tc"
+            else ops.plan_splits(lens_host, s.block_size, device=dev))
     D = s.head_dim
     ctx = torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
-    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, nb_local, s.q_heads, s.value_dim),
+    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, nb_local, s.q_heads, s.latent_dim,
+                                                s.value_dim),
                      dtype=torch.uint8, device=dev)
     want_lse = split_k
     gathered_ctx = torch.empty((world, nb_local, s.q_heads, D), dtype=torch.float32,
@@ -323,9 +309,8 @@ def run_ours(args, s, rank: int, world: int):
                               phase="combine")
         res = ctx
         if split_k:
-            dist.all_gather_into_tensor(gathered_ctx, ctx)
-            dist.all_gather_into_tensor(gathered_lse, r["lse"])
-            res, _ = ops.lse_merge(gathered_ctx, gathered_lse)
+            res = mg.gather_and_merge(ctx, r["lse"], world, lambda c, l: ops.lse_merge(c, l)[0],
+                                      gathered_ctx, gathered_lse)
         if w_o is not None:
             if wo_ws is None:
                 wo_ws = torch.empty(1, dtype=torch.uint8, device=dev)

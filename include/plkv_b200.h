@@ -130,6 +130,18 @@ int plkv_plan_splits(const int32_t* seq_lens_host, int32_t batch, int32_t block_
                      int32_t target_items, int32_t min_blocks, plkv_work_item* items_host,
                      int32_t max_items, int32_t* seq_item_begin_host, int32_t* n_items_host);
 
+/* Host-side balanced planner for the persistent tensor-core decode: the
+ * blocks of all sequences, in sequence order, are cut into `n_workers`
+ * contiguous ranges of equal size (+-1 block); every (worker, sequence)
+ * overlap becomes one item.  Worker w processes items
+ * worker_item_begin_host[w] .. [w+1] in order; items are ordered by sequence
+ * as for plkv_plan_splits (seq_item_begin_host has batch + 1 entries) and a
+ * sequence of length 0 still gets one empty item.  Same return codes. */
+int plkv_plan_workers(const int32_t* seq_lens_host, int32_t batch, int32_t block_size,
+                      int32_t n_workers, plkv_work_item* items_host, int32_t max_items,
+                      int32_t* seq_item_begin_host, int32_t* worker_item_begin_host,
+                      int32_t* n_items_host);
+
 /* ------------------------------------------------------------------ decode */
 
 /* Query projection q_lat[b, h, :] = W_k[kv(h)] q[b, h, :] with W_k head-major
@@ -153,9 +165,11 @@ typedef struct plkv_latent_decode_args {
     const int32_t* block_tables;  /* [batch, max_blocks] physical block ids */
     int64_t max_blocks;
     const int32_t* seq_lens;      /* [batch] active lengths */
-    const plkv_work_item* items;  /* [n_items] from plkv_plan_splits, on the device */
+    const plkv_work_item* items;  /* [n_items] from a planner, on the device */
     const int32_t* seq_item_begin;/* [batch + 1] on the device */
     int32_t n_items;
+    const int32_t* worker_item_begin; /* [n_workers + 1] from plkv_plan_workers, or NULL */
+    int32_t n_workers;            /* tensor-core mode: persistent CTA pairs (0: one per item) */
     int32_t allow_empty;          /* 1: a sequence of length 0 yields ctx 0, lse -inf */
     const float* w_v;             /* [proj_heads, value_dim, head_dim] or NULL (latent ctx out) */
     int32_t proj_heads;
@@ -171,9 +185,10 @@ typedef struct plkv_latent_decode_args {
     int32_t* err_flags;           /* optional */
 } plkv_latent_decode_args;
 
-/* Workspace bytes the decode needs for `n_items` items. */
+/* Workspace bytes the decode needs for `n_items` items (either mode; it
+ * includes the FP16 copy of the query used by the tensor-core mode). */
 size_t plkv_latent_decode_workspace_size(int32_t n_items, int32_t batch, int32_t q_heads,
-                                         int32_t value_dim);
+                                         int32_t latent_dim, int32_t value_dim);
 
 /* Direct paged latent decode: split-K partial pass over the work items
  * (scores, active-length mask, online softmax, latent context), then the
@@ -200,7 +215,7 @@ int plkv_latent_decode_combine(const plkv_latent_decode_args* args, plkv_stream_
  * file-scope device array of PLKV_NOALLOC_SCRATCH_BYTES that every GPU loading
  * the library holds until exit.  Returns PLKV_ERR_WORKSPACE, launching
  * nothing, when plkv_latent_decode_workspace_size(n_items, batch, q_heads,
- * value_dim) exceeds that size (plan fewer work items).  Calls no cudaMalloc
+ * latent_dim, value_dim) exceeds that size (plan fewer work items).  Calls no cudaMalloc
  * or cudaFree.  The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call
  * before any stream capture.  All calls share the array, so calls that overlap

@@ -51,8 +51,8 @@ class LatentDecodeArgs(ctypes.Structure):
         ("q_lat", _P), ("cache", _P), ("num_physical", _I64), ("block_size", _I32),
         ("latent_dim", _I32), ("value_dim", _I32), ("batch", _I32), ("q_heads", _I32),
         ("scale", _F), ("block_tables", _P), ("max_blocks", _I64), ("seq_lens", _P),
-        ("items", _P), ("seq_item_begin", _P), ("n_items", _I32), ("allow_empty", _I32),
-        ("w_v", _P), ("proj_heads", _I32), ("head_dim", _I32), ("ctx", _P), ("lse", _P),
+        ("items", _P), ("seq_item_begin", _P), ("n_items", _I32),
+        ("worker_item_begin", _P), ("n_workers", _I32), ("allow_empty", _I32), ("w_v", _P), ("proj_heads", _I32), ("head_dim", _I32), ("ctx", _P), ("lse", _P),
         ("scores", _P), ("probs", _P), ("max_seq_len", _I32), ("mode", _I32),
         ("workspace", _P), ("workspace_bytes", _SZ), ("err_flags", _P),
     ]
@@ -80,8 +80,9 @@ SIGNATURES = {
     "plkv_kv_append_f16": (ctypes.c_int, [_P, _P, _P, _I64, _P, _P, _P, _I64, _P, _P, _I64, _I32,
                                           _I32, _I32, _P, _P]),
     "plkv_plan_splits": (ctypes.c_int, [_P, _I32, _I32, _I32, _I32, _P, _I32, _P, _P]),
+    "plkv_plan_workers": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _I32, _P, _P, _P]),
     "plkv_project_query": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P]),
-    "plkv_latent_decode_workspace_size": (_SZ, [_I32, _I32, _I32, _I32]),
+    "plkv_latent_decode_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
     "plkv_latent_decode": (ctypes.c_int, [ctypes.POINTER(LatentDecodeArgs), _P]),
     "plkv_latent_decode_partial": (ctypes.c_int, [ctypes.POINTER(LatentDecodeArgs), _P]),
     "plkv_latent_decode_combine": (ctypes.c_int, [ctypes.POINTER(LatentDecodeArgs), _P]),

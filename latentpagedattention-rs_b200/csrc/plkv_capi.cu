@@ -169,6 +169,60 @@ int plkv_plan_splits(const int32_t* seq_lens_host, int32_t batch, int32_t block_
     return PLKV_OK;
 }
 
+int plkv_plan_workers(const int32_t* seq_lens_host, int32_t batch, int32_t block_size,
+                      int32_t n_workers, plkv_work_item* items_host, int32_t max_items,
+                      int32_t* seq_item_begin_host, int32_t* worker_item_begin_host,
+                      int32_t* n_items_host) {
+    if (batch <= 0 || block_size <= 0 || n_workers <= 0) return PLKV_ERR_ZERO_VALUE;
+    if (!seq_lens_host || !n_items_host) return PLKV_ERR_INVALID_ARGUMENT;
+    std::vector<int64_t> nb(batch), start(batch + 1, 0);
+    for (int b = 0; b < batch; ++b) {
+        if (seq_lens_host[b] < 0) return PLKV_ERR_INVALID_ARGUMENT;
+        nb[b] = (seq_lens_host[b] + block_size - 1) / block_size;
+        start[b + 1] = start[b] + nb[b];
+    }
+    const int64_t total = start[batch];
+    // Worker w owns global blocks [bound(w), bound(w+1)).
+    auto bound = [&](int64_t w) { return total * w / n_workers; };
+    std::vector<plkv_work_item> items;
+    std::vector<int32_t> item_worker;
+    std::vector<int32_t> seq_begin(batch + 1, 0);
+    int64_t w = 0;
+    for (int b = 0; b < batch; ++b) {
+        seq_begin[b] = (int32_t)items.size();
+        if (nb[b] == 0) {
+            // Empty sequence: one empty item, on the worker owning this position.
+            while (w + 1 < n_workers && bound(w + 1) <= start[b]) ++w;
+            items.push_back({b, 0, 0, 0});
+            item_worker.push_back((int32_t)w);
+            continue;
+        }
+        int64_t pos = start[b];
+        while (pos < start[b + 1]) {
+            while (bound(w + 1) <= pos) ++w;
+            const int64_t end = std::min(start[b + 1], bound(w + 1));
+            items.push_back({b, (int32_t)(pos - start[b]), (int32_t)(end - start[b]), 0});
+            item_worker.push_back((int32_t)w);
+            pos = end;
+        }
+    }
+    seq_begin[batch] = (int32_t)items.size();
+    *n_items_host = (int32_t)items.size();
+    if ((int64_t)items.size() > max_items || !items_host || !seq_item_begin_host ||
+        !worker_item_begin_host)
+        return PLKV_ERR_WORKSPACE;
+    std::copy(items.begin(), items.end(), items_host);
+    std::copy(seq_begin.begin(), seq_begin.end(), seq_item_begin_host);
+    // Items are in worker order already (workers take consecutive ranges).
+    int32_t k = 0;
+    for (int32_t ww = 0; ww <= n_workers; ++ww) {
+        while (k < (int32_t)items.size() && item_worker[k] < ww) ++k;
+        worker_item_begin_host[ww] = k;
+    }
+    worker_item_begin_host[n_workers] = (int32_t)items.size();
+    return PLKV_OK;
+}
+
 int plkv_project_query(const float* q, const float* w_k, float* q_lat, int32_t batch,
                        int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t latent_dim,
                        plkv_stream_t stream) {
@@ -184,9 +238,9 @@ int plkv_project_query(const float* q, const float* w_k, float* q_lat, int32_t b
 }
 
 size_t plkv_latent_decode_workspace_size(int32_t n_items, int32_t batch, int32_t q_heads,
-                                         int32_t value_dim) {
-    if (n_items <= 0 || batch <= 0 || q_heads <= 0 || value_dim <= 0) return 0;
-    return decode_workspace_bytes(n_items, batch, q_heads, value_dim);
+                                         int32_t latent_dim, int32_t value_dim) {
+    if (n_items <= 0 || batch <= 0 || q_heads <= 0 || latent_dim <= 0 || value_dim <= 0) return 0;
+    return decode_workspace_bytes(n_items, batch, q_heads, latent_dim, value_dim);
 }
 
 static int validate_latent(const plkv_latent_decode_args* a) {
@@ -208,8 +262,10 @@ static int validate_latent(const plkv_latent_decode_args* a) {
     if (a->n_items > 65535) return PLKV_ERR_UNSUPPORTED;  // grid y of the partial pass
     if ((int64_t)a->max_blocks * a->block_size > 0x7fffffffLL) return PLKV_ERR_ARITHMETIC_OVERFLOW;
     if (a->workspace_bytes <
-        decode_workspace_bytes(a->n_items, a->batch, a->q_heads, a->value_dim))
+        decode_workspace_bytes(a->n_items, a->batch, a->q_heads, a->latent_dim, a->value_dim))
         return PLKV_ERR_WORKSPACE;
+    if (a->n_workers < 0 || (a->n_workers > 0 && !a->worker_item_begin))
+        return PLKV_ERR_INVALID_ARGUMENT;
     if (a->mode != PLKV_MODE_EXACT_F32 && a->mode != PLKV_MODE_TC_F16) return PLKV_ERR_UNSUPPORTED;
     return PLKV_OK;
 }
@@ -218,7 +274,7 @@ int plkv_latent_decode_partial(const plkv_latent_decode_args* a, plkv_stream_t s
     int st = validate_latent(a);
     if (st != PLKV_OK) return st;
     DecodeWorkspace ws = carve_workspace(a->workspace, a->n_items, a->batch, a->q_heads,
-                                         a->value_dim);
+                                         a->latent_dim, a->value_dim);
     cudaError_t e;
     if (a->mode == PLKV_MODE_TC_F16) {
         if (!tc_supported(*a)) return PLKV_ERR_UNSUPPORTED;
@@ -233,7 +289,7 @@ int plkv_latent_decode_combine(const plkv_latent_decode_args* a, plkv_stream_t s
     int st = validate_latent(a);
     if (st != PLKV_OK) return st;
     DecodeWorkspace ws = carve_workspace(a->workspace, a->n_items, a->batch, a->q_heads,
-                                         a->value_dim);
+                                         a->latent_dim, a->value_dim);
     cudaStream_t s = (cudaStream_t)stream;
     PLKV_CUDA_CHECK(launch_combine(ws, a->seq_item_begin, a->batch, a->q_heads, a->value_dim,
                                    a->w_v, a->proj_heads, a->head_dim, a->ctx, a->lse, s));
@@ -283,7 +339,7 @@ int plkv_out_proj(const float* x, const float* w_o, float* out, int32_t batch, i
 size_t plkv_fullkv_decode_workspace_size(int32_t n_items, int32_t batch, int32_t q_heads,
                                          int32_t head_dim) {
     if (n_items <= 0 || batch <= 0 || q_heads <= 0 || head_dim <= 0) return 0;
-    return decode_workspace_bytes(n_items, batch, q_heads, head_dim);
+    return decode_workspace_bytes(n_items, batch, q_heads, 0, head_dim);
 }
 
 int plkv_fullkv_decode(const plkv_fullkv_decode_args* a, plkv_stream_t stream) {
@@ -301,9 +357,9 @@ int plkv_fullkv_decode(const plkv_fullkv_decode_args* a, plkv_stream_t stream) {
         return PLKV_ERR_UNSUPPORTED;
     if ((int64_t)a->max_blocks * a->block_size > 0x7fffffffLL) return PLKV_ERR_ARITHMETIC_OVERFLOW;
     if (a->workspace_bytes <
-        decode_workspace_bytes(a->n_items, a->batch, a->q_heads, a->head_dim))
+        decode_workspace_bytes(a->n_items, a->batch, a->q_heads, 0, a->head_dim))
         return PLKV_ERR_WORKSPACE;
-    DecodeWorkspace ws = carve_workspace(a->workspace, a->n_items, a->batch, a->q_heads,
+    DecodeWorkspace ws = carve_workspace(a->workspace, a->n_items, a->batch, a->q_heads, 0,
                                          a->head_dim);
     cudaStream_t s = (cudaStream_t)stream;
     PLKV_CUDA_CHECK(launch_fullkv_partial_exact(*a, ws, s));

@@ -52,24 +52,27 @@ __device__ __forceinline__ float warp_sum(float v) {
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Workspace of one decode call: per-item partial softmax state and context,
-// and per-row (sequence, head) final max / sum used to emit probabilities.
+// per-row (sequence, head) final max / sum used to emit probabilities, and
+// the FP16 pre-scaled query the tensor-core pass loads by TMA.
 struct DecodeWorkspace {
     float* part_m;    // [n_items, q_heads]   running max of the item's scores
     float* part_l;    // [n_items, q_heads]   sum of exp(score - part_m)
     float* part_ctx;  // [n_items, q_heads, width] unnormalised context
     float* row_m;     // [batch, q_heads]
     float* row_l;     // [batch, q_heads]
+    uint16_t* q16;    // [batch, q_heads, latent] FP16 (latent = 0: absent)
 };
 
 __host__ __device__ inline size_t decode_workspace_bytes(int n_items, int batch, int q_heads,
-                                                         int width) {
+                                                         int latent, int width) {
     size_t nh = size_t(n_items) * q_heads;
     return align256(nh * 4) * 2 + align256(nh * size_t(width) * 4) +
-           align256(size_t(batch) * q_heads * 4) * 2;
+           align256(size_t(batch) * q_heads * 4) * 2 +
+           align256(size_t(batch) * q_heads * size_t(latent) * 2);
 }
 
 inline DecodeWorkspace carve_workspace(void* base, int n_items, int batch, int q_heads,
-                                       int width) {
+                                       int latent, int width) {
     char* p = static_cast<char*>(base);
     size_t nh = size_t(n_items) * q_heads;
     DecodeWorkspace w;
@@ -82,6 +85,8 @@ inline DecodeWorkspace carve_workspace(void* base, int n_items, int batch, int q
     w.row_m = reinterpret_cast<float*>(p);
     p += align256(size_t(batch) * q_heads * 4);
     w.row_l = reinterpret_cast<float*>(p);
+    p += align256(size_t(batch) * q_heads * 4);
+    w.q16 = latent > 0 ? reinterpret_cast<uint16_t*>(p) : nullptr;
     return w;
 }
 

@@ -9,31 +9,36 @@
 // sum_t exp(score_t - m) L_t[:512]; the shared combine pass merges items and
 // applies W_uv.  Scores are (L . q_lat) * scale as in lib.rs:1033-1041.
 //
-// Work split: a cluster of two CTAs (a tcgen05 CTA pair) processes one item
-// in tiles of 64 tokens.  CTA r owns query heads [64r, 64r+64).
+// Work split.  A cluster of two CTAs (a tcgen05 CTA pair) is persistent: it
+// processes the items of one worker of plkv_plan_workers (or one item) in
+// tiles of 64 tokens.  CTA r owns query heads [64r, 64r+64).
 //   S = Q . L^T  : cta_group::2 MMA, M = 128 heads, N = 64 tokens, K = 576.
 //                  CTA r supplies its heads' Q and tokens [32r, 32r+32) of L;
-//                  TMEM of CTA r receives its 64 heads x 64 tokens (32 cols).
+//                  its TMEM receives its 64 heads x 64 tokens (32 columns).
 //   O += P . V   : cta_group::2 MMA, M = 128 heads, N = 256 value columns
 //                  (two instructions), K = 64 tokens.  CTA r supplies its
 //                  heads' P and value columns {0,1,4,5} (r = 0) or {2,3,6,7}
-//                  (r = 1) in 64-column blocks; TMEM of CTA r holds its 64
-//                  heads x 512 columns in 256 columns.
-// Because the two MMAs need different slices of the tile at identical
-// shared-memory offsets in both CTAs, each CTA loads its own token half of
-// all nine 64-column blocks ("K region") and both token halves of its four
-// value blocks ("V region"): 17 TMA boxes of 32 rows x 64 columns per tile.
+//                  (r = 1) in 64-column blocks; its TMEM holds its 64 heads x
+//                  512 columns in 256 columns.
+// The two MMAs need different slices of a tile at identical shared-memory
+// offsets in both CTAs, so each CTA loads its own token half of all nine
+// 64-column blocks into the K ring (consumed by S, released when S is done)
+// and both token halves of its four value blocks into the V ring (consumed by
+// O): 17 TMA boxes of 32 rows x 64 columns per tile and CTA.  Decoupling the
+// rings lets the next tiles' K loads start as soon as S completes.
 //
-// Softmax runs in the log2 domain (the query is pre-scaled by
-// scale * log2(e)).  The running max is updated lazily: probabilities are
-// taken against a stale max until a tile's max exceeds it by more than 8
-// (probabilities stay <= 2^8 in FP16); only then is the accumulated O
-// rescaled in TMEM.  The two threads that share a head (token halves) agree on
-// every decision through shared memory, and TMEM lane = head, so no
-// exchange between the two CTAs is needed.
+// The query is converted once per call (q_prep kernel) to FP16 pre-scaled by
+// scale * log2(e) and loaded per item by TMA.  Softmax runs in the log2
+// domain with a lazily updated running max: probabilities are taken against a
+// stale max until a tile's max exceeds it by more than 8 (probabilities stay
+// <= 2^8 in FP16); only then is the accumulated O rescaled in TMEM.  TMEM lane
+// = head, and the two threads sharing a head (token halves) agree through
+// shared memory, so the CTAs never exchange softmax state.
 //
-// Every barrier wait is bounded (1 s): on expiry the kernel records
-// PLKV_FLAG_TIMEOUT, abandons the item, releases its tensor memory and exits.
+// Warp roles per CTA: 0 = Q and K loads, 1 = TMEM allocation and (leader CTA)
+// MMA issue, 2 = V loads, 4..7 = softmax and epilogue.  Every barrier wait is
+// bounded (1 s): on expiry the kernel records PLKV_FLAG_TIMEOUT, abandons its
+// work, releases tensor memory and exits.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -48,30 +53,46 @@ constexpr int kHeadsPerCta = 64;
 constexpr int kLatent = 576;
 constexpr int kValue = 512;
 constexpr int kTile = 64;
-constexpr int kKBlocks = kLatent / 64;                  // 9
-constexpr uint32_t kBox = 32 * 128;                      // 32 rows x 64 FP16 = 4 KiB
-constexpr uint32_t kQBytes = kKBlocks * kHeadsPerCta * 128;  // 72 KiB
-constexpr uint32_t kKRegion = kKBlocks * kBox;           // 36 KiB
-constexpr uint32_t kVRegion = 2 * 4 * kBox;              // 32 KiB
-constexpr uint32_t kStageBytes = kKRegion + kVRegion;    // 68 KiB
+constexpr int kKBlocks = kLatent / 64;                       // 9
+constexpr uint32_t kBox = 32 * 128;                           // 32 rows x 64 FP16
+constexpr uint32_t kQAtom = kHeadsPerCta * 128;               // 64 rows x 64 FP16
+constexpr uint32_t kQBytes = kKBlocks * kQAtom;               // 72 KiB
+constexpr uint32_t kKStage = kKBlocks * kBox;                 // 36 KiB
+constexpr uint32_t kVStage = 2 * 4 * kBox;                    // 32 KiB
 constexpr int kStages = 2;
-constexpr uint32_t kPBytes = kHeadsPerCta * kTile * 2;   // 8 KiB
+constexpr uint32_t kPBytes = kHeadsPerCta * kTile * 2;        // 8 KiB
 constexpr uint32_t kQOff = 0;
-constexpr uint32_t kStageOff = kQOff + kQBytes;
-constexpr uint32_t kPOff = kStageOff + kStages * kStageBytes;
-constexpr uint32_t kMiscOff = kPOff + 2 * kPBytes;       // 229376
+constexpr uint32_t kKOff = kQOff + kQBytes;
+constexpr uint32_t kVOff = kKOff + kStages * kKStage;
+constexpr uint32_t kPOff = kVOff + kStages * kVStage;
+constexpr uint32_t kMiscOff = kPOff + 2 * kPBytes;            // 229376
 constexpr uint32_t kMiscBytes = 2048;
-constexpr uint32_t kSmemBytes = kMiscOff + kMiscBytes;   // 231424
-constexpr uint32_t kTxBytes = 2u * 17u * kBox;           // both CTAs, one tile
+constexpr uint32_t kSmemBytes = kMiscOff + kMiscBytes;        // 231424
+constexpr uint32_t kQTx = 2u * kQBytes;                       // both CTAs
+constexpr uint32_t kKTx = 2u * kKStage;                       // both CTAs
+constexpr uint32_t kVTx = kVStage;                            // own CTA
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemO = 64;                          // S buffers at 0 and 32
+constexpr uint32_t kTmemO = 64;                               // S buffers at 0 and 32
 constexpr float kTau = 8.f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-// Misc region offsets.
-constexpr uint32_t kBarFull = 0, kBarKEmpty = 16, kBarSFull = 32, kBarPFull = 48, kBarODone = 64;
-constexpr uint32_t kTmemSlot = 80, kAbort = 84, kRedMax = 128, kRedSum = 128 + 2 * 128 * 4;
-
+// Misc region: barriers (8 bytes each), then small shared arrays.
+enum : uint32_t {
+    kBarQFull = 0,     // leader: Q of the item landed in both CTAs
+    kBarQFree = 8,     // both: every MMA of the item completed (Q may be reloaded)
+    kBarKFull = 16,    // [2] leader: K tile landed in both CTAs
+    kBarKEmpty = 32,   // [2] both: S of the tile completed
+    kBarVFull = 48,    // [2] own: V tile landed in this CTA
+    kBarVEmpty = 64,   // [2] both: O of the tile completed (V reusable)
+    kBarSFull = 80,    // [2] both: S of the tile in TMEM
+    kBarPFull = 96,    // [2] leader: P written (and V checked) in both CTAs
+    kBarODone = 112,   // [2] both: O of the tile completed (P buffer reusable)
+    kBarOFree = 128,   // leader: epilogue of the item read O in both CTAs
+    kTmemSlot = 136,
+    kAbort = 140,
+    kRedMax = 256,     // [2][128] float
+    kRedSum = 256 + 1024,
+};
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 static_assert(kRedSum + 128 * 4 <= kMiscBytes, "misc region");
 
@@ -79,12 +100,66 @@ __device__ __forceinline__ void named_sync_softmax() {
     asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Plain (one-CTA) tile load that completes on a barrier of this CTA.
+__device__ __forceinline__ void tma_load_2d_own(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        : "memory");
+}
+
+struct ItemGeom {
+    int seq, t_begin, t_end, n_tiles;
+};
+
+__device__ __forceinline__ ItemGeom item_geom(const plkv_work_item* items, int idx,
+                                              const int32_t* seq_lens, int bs, int64_t cap,
+                                              int32_t* flags, bool report) {
+    const plkv_work_item it = items[idx];
+    ItemGeom g;
+    g.seq = it.seq;
+    int len = seq_lens[it.seq];
+    if (len < 0 || len > cap) {
+        if (report) set_flag(flags, PLKV_FLAG_BAD_LENGTH);
+        len = len < 0 ? 0 : (int)cap;
+    }
+    g.t_begin = it.block_begin * bs;
+    g.t_end = max(g.t_begin, min(it.block_end * bs, len));
+    g.n_tiles = (g.t_end - g.t_begin + kTile - 1) / kTile;
+    return g;
+}
+
+// Pool row of the first token of half-tile `h` of tile `j` (a half past the
+// end reuses half 0 so that every load reads valid pool rows).
+__device__ __forceinline__ int half_row(const ItemGeom& g, int j, int h,
+                                        const int32_t* __restrict__ tables, int64_t max_blocks,
+                                        int64_t num_physical, int bs, int32_t* flags) {
+    int hs = g.t_begin + kTile * j + 32 * h;
+    if (hs >= g.t_end) hs = g.t_begin + kTile * j;
+    const int lb = hs / bs;
+    int32_t phys = tables[(int64_t)g.seq * max_blocks + lb];
+    if (phys < 0 || phys >= num_physical) {
+        set_flag(flags, PLKV_FLAG_BAD_BLOCK);
+        phys = 0;
+    }
+    return phys * bs + (hs - lb * bs);
+}
+
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
-latent_partial_tc_kernel(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ q_lat,
-                         float qscale, int bs, const int32_t* __restrict__ tables,
-                         int64_t max_blocks, int64_t num_physical,
-                         const int32_t* __restrict__ seq_lens,
-                         const plkv_work_item* __restrict__ items, DecodeWorkspace ws,
+latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
+                         const __grid_constant__ CUtensorMap q_map, int bs,
+                         const int32_t* __restrict__ tables, int64_t max_blocks,
+                         int64_t num_physical, const int32_t* __restrict__ seq_lens,
+                         const plkv_work_item* __restrict__ items,
+                         const int32_t* __restrict__ worker_item_begin, DecodeWorkspace ws,
                          int32_t* flags) {
     using namespace sm100;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -96,63 +171,41 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
-    const int item = blockIdx.x >> 1;
+    const int worker = blockIdx.x >> 1;
+    const int i_begin = worker_item_begin ? worker_item_begin[worker] : worker;
+    const int i_end = worker_item_begin ? worker_item_begin[worker + 1] : worker + 1;
+    const int64_t cap = max_blocks * (int64_t)bs;
+
     uint8_t* misc = smem + kMiscOff;
-    const uint32_t mbase = sbase + kMiscOff;
-    const uint32_t bar_full = mbase + kBarFull, bar_kempty = mbase + kBarKEmpty;
-    const uint32_t bar_sfull = mbase + kBarSFull, bar_pfull = mbase + kBarPFull;
-    const uint32_t bar_odone = mbase + kBarODone;
+    const uint32_t mb = sbase + kMiscOff;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + kAbort);
     float* red_max = reinterpret_cast<float*>(misc + kRedMax);
     float* red_sum = reinterpret_cast<float*>(misc + kRedSum);
 
     if (tid == 0) {
+        mbar_init(mb + kBarQFull, 1);
+        mbar_init(mb + kBarQFree, 1);
+        mbar_init(mb + kBarOFree, 2);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(bar_full + 8 * i, 1);
-            mbar_init(bar_kempty + 8 * i, 1);
-            mbar_init(bar_sfull + 8 * i, 1);
-            mbar_init(bar_pfull + 8 * i, 8);  // 4 softmax warps x 2 CTAs
-            mbar_init(bar_odone + 8 * i, 1);
+            mbar_init(mb + kBarKFull + 8 * i, 1);
+            mbar_init(mb + kBarKEmpty + 8 * i, 1);
+            mbar_init(mb + kBarVFull + 8 * i, 1);
+            mbar_init(mb + kBarVEmpty + 8 * i, 1);
+            mbar_init(mb + kBarSFull + 8 * i, 1);
+            mbar_init(mb + kBarPFull + 8 * i, 2);
+            mbar_init(mb + kBarODone + 8 * i, 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc_pair(sbase + kMiscOff + kTmemSlot, kTmemCols);
+        tmem_alloc_pair(mb + kTmemSlot, kTmemCols);
         tmem_relinquish_pair();
     }
-    if (warp == 0 && lane == 0) prefetch_tensormap(&tmap);
-
-    // Item geometry (same in every thread).
-    const plkv_work_item it = items[item];
-    const int b = it.seq;
-    const int64_t cap = max_blocks * (int64_t)bs;
-    int len = seq_lens[b];
-    if (len < 0 || len > cap) {
-        if (tid == 0 && leader) set_flag(flags, PLKV_FLAG_BAD_LENGTH);
-        len = len < 0 ? 0 : (int)cap;
+    if (warp == 0 && lane == 0) {
+        prefetch_tensormap(&cache_map);
+        prefetch_tensormap(&q_map);
     }
-    const int t_begin = it.block_begin * bs;
-    const int t_end = max(t_begin, min(it.block_end * bs, len));
-    const int n_tiles = (t_end - t_begin + kTile - 1) / kTile;
-
-    // Q of this CTA's 64 heads, scaled into log2 units, FP16, 128-byte swizzle:
-    // nine atoms of [64 heads x 64 columns].
-    {
-        const float* qsrc = q_lat + ((int64_t)b * kHeads + kHeadsPerCta * rank) * kLatent;
-        for (int i = tid; i < kHeadsPerCta * (kLatent / 4); i += 256) {
-            const int r = i / (kLatent / 4), col = (i - r * (kLatent / 4)) * 4;
-            const float4 v = __ldg(reinterpret_cast<const float4*>(qsrc + (int64_t)r * kLatent + col));
-            const __half2 h01 = __floats2half2_rn(v.x * qscale, v.y * qscale);
-            const __half2 h23 = __floats2half2_rn(v.z * qscale, v.w * qscale);
-            uint2 pk;
-            pk.x = *reinterpret_cast<const uint32_t*>(&h01);
-            pk.y = *reinterpret_cast<const uint32_t*>(&h23);
-            *reinterpret_cast<uint2*>(smem + kQOff + (col >> 6) * (kHeadsPerCta * 128) +
-                                      sw128_offset(r, col & 63)) = pk;
-        }
-    }
-    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     cluster_sync();
@@ -160,87 +213,133 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(misc + kTmemSlot);
 
     if (warp == 0) {
-        // ------------------------------------------------------ TMA producer
-        const uint64_t pol = policy_evict_first();
-        const uint32_t full_leader0 = mapa(bar_full, 0), full_leader1 = mapa(bar_full + 8, 0);
-        for (int j = 0; j < n_tiles; ++j) {
-            const int st = j & 1;
-            int y = 0;
-            if (lane < 2) {
-                int hs = t_begin + kTile * j + 32 * lane;
-                if (hs >= t_end) hs = t_begin + kTile * j;  // half beyond the end: reuse half 0
-                const int lb = hs / bs;
-                int32_t phys = tables[(int64_t)b * max_blocks + lb];
-                if (phys < 0 || phys >= num_physical) {
-                    set_flag(flags, PLKV_FLAG_BAD_BLOCK);
-                    phys = 0;
-                }
-                y = phys * bs + (hs - lb * bs);
-            }
-            const int y0 = __shfl_sync(0xffffffffu, y, 0);
-            const int y1 = __shfl_sync(0xffffffffu, y, 1);
-            int ok = 1;
-            if (lane == 0) {
-                if (j >= 2) ok = mbar_wait(bar_kempty + 8 * st, ((j - 2) >> 1) & 1, flags, abort_flag);
-                if (ok) {
-                    if (leader) mbar_arrive_expect_tx(bar_full + 8 * st, kTxBytes);
-                    const uint32_t stage = sbase + kStageOff + st * kStageBytes;
-                    const uint32_t fb = st ? full_leader1 : full_leader0;
-                    const int yown = rank ? y1 : y0;
+        // ---------------------------------------------------- Q and K loads
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            const uint32_t kfull0 = mapa(mb + kBarKFull, 0), kfull1 = mapa(mb + kBarKFull + 8, 0);
+            const uint32_t qfull = mapa(mb + kBarQFull, 0);
+            int gt = 0;  // tile counter over the worker's items
+            bool ok = true;
+            for (int ii = i_begin; ok && ii < i_end; ++ii) {
+                const ItemGeom g = item_geom(items, ii, seq_lens, bs, cap, flags, false);
+                const int ni = ii - i_begin;
+                auto load_q = [&]() -> bool {
+                    if (ni >= 1 &&
+                        !mbar_wait(mb + kBarQFree, (ni - 1) & 1, flags, abort_flag))
+                        return false;
+                    if (leader) mbar_arrive_expect_tx(mb + kBarQFull, kQTx);
+                    const int y = g.seq * kHeads + kHeadsPerCta * (int)rank;
                     for (int c = 0; c < kKBlocks; ++c)
-                        tma_load_2d_pair(stage + c * kBox, &tmap, c * 64, yown, fb, pol);
+                        tma_load_2d_pair(sbase + kQOff + c * kQAtom, &q_map, c * 64, y, qfull, pol);
+                    return true;
+                };
+                // The first K tiles of an item only need free K stages; Q waits
+                // for every MMA of the previous item, so load it after them.
+                const int pre = min(2, g.n_tiles);
+                for (int j = 0; ok && j < g.n_tiles; ++j) {
+                    if (j == pre && !(ok = load_q())) break;
+                    const int gj = gt + j, st = gj & 1;
+                    if (gj >= 2 && !(ok = mbar_wait(mb + kBarKEmpty + 8 * st, ((gj - 2) >> 1) & 1,
+                                                    flags, abort_flag)))
+                        break;
+                    const int y = half_row(g, j, (int)rank, tables, max_blocks, num_physical, bs, flags);
+                    if (leader) mbar_arrive_expect_tx(mb + kBarKFull + 8 * st, kKTx);
+                    const uint32_t dst = sbase + kKOff + st * kKStage;
+                    const uint32_t fb = st ? kfull1 : kfull0;
+                    for (int c = 0; c < kKBlocks; ++c)
+                        tma_load_2d_pair(dst + c * kBox, &cache_map, c * 64, y, fb, pol);
+                }
+                if (ok && pre == g.n_tiles) ok = load_q();
+                gt += g.n_tiles;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        // --------------------------------------------------------- V loads
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            int gt = 0;
+            bool ok = true;
+            for (int ii = i_begin; ok && ii < i_end; ++ii) {
+                const ItemGeom g = item_geom(items, ii, seq_lens, bs, cap, flags, false);
+                for (int j = 0; j < g.n_tiles; ++j) {
+                    const int gj = gt + j, st = gj & 1;
+                    if (gj >= 2 && !(ok = mbar_wait(mb + kBarVEmpty + 8 * st, ((gj - 2) >> 1) & 1,
+                                                    flags, abort_flag)))
+                        break;
+                    const int y0 = half_row(g, j, 0, tables, max_blocks, num_physical, bs, flags);
+                    const int y1 = half_row(g, j, 1, tables, max_blocks, num_physical, bs, flags);
+                    mbar_arrive_expect_tx(mb + kBarVFull + 8 * st, kVTx);
+                    const uint32_t dst = sbase + kVOff + st * kVStage;
                     for (int h = 0; h < 2; ++h)
                         for (int s = 0; s < 4; ++s) {
                             const int cb = (s >> 1) * 4 + (s & 1) + 2 * (int)rank;
-                            tma_load_2d_pair(stage + kKRegion + h * 4 * kBox + s * kBox, &tmap,
-                                             cb * 64, h ? y1 : y0, fb, pol);
+                            tma_load_2d_own(dst + h * 4 * kBox + s * kBox, &cache_map, cb * 64,
+                                            h ? y1 : y0, mb + kBarVFull + 8 * st, pol);
                         }
                 }
+                gt += g.n_tiles;
             }
-            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         }
+        __syncwarp();
     } else if (warp == 1) {
         // ---------------------------------------------- MMA issue (leader)
-        if (leader && lane == 0 && n_tiles > 0) {
+        if (leader && lane == 0) {
             const uint32_t id_s = idesc_f16(128, 64, false, false);
             const uint32_t id_o = idesc_f16(128, 256, false, true);
-            auto issue_s = [&](int j) -> bool {
-                const int st = j & 1;
-                if (!mbar_wait(bar_full + 8 * st, (j >> 1) & 1, flags, abort_flag)) return false;
+            auto issue_s = [&](int gs) -> bool {
+                const int st = gs & 1;
+                if (!mbar_wait(mb + kBarKFull + 8 * st, (gs >> 1) & 1, flags, abort_flag))
+                    return false;
                 tc_fence_after();
-                const uint32_t kreg = sbase + kStageOff + st * kStageBytes;
-                const uint32_t d = tmem + 32 * st;
+                const uint32_t kreg = sbase + kKOff + st * kKStage;
 #pragma unroll 4
                 for (int k = 0; k < kKBlocks * 4; ++k) {
-                    const uint64_t a = sdesc_sw128(sbase + kQOff + (k >> 2) * (kHeadsPerCta * 128) +
-                                                       (k & 3) * 32, 16, 1024);
-                    const uint64_t bd = sdesc_sw128(kreg + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
-                    mma_pair_f16(d, a, bd, id_s, k > 0 ? 1u : 0u);
+                    const uint64_t a = sdesc_sw128(sbase + kQOff + (k >> 2) * kQAtom + (k & 3) * 32,
+                                                   16, 1024);
+                    const uint64_t b = sdesc_sw128(kreg + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
+                    mma_pair_f16(tmem + 32 * st, a, b, id_s, k > 0 ? 1u : 0u);
                 }
-                mma_commit_pair(bar_sfull + 8 * st, 0x3);
+                mma_commit_pair(mb + kBarSFull + 8 * st, 0x3);
+                mma_commit_pair(mb + kBarKEmpty + 8 * st, 0x3);
                 return true;
             };
-            bool ok = issue_s(0);
-            if (ok && n_tiles > 1) ok = issue_s(1);
-            for (int j = 0; ok && j < n_tiles; ++j) {
-                const int st = j & 1;
-                if (!mbar_wait(bar_pfull + 8 * st, (j >> 1) & 1, flags, abort_flag)) break;
+            int gt = 0;
+            bool ok = true;
+            for (int ii = i_begin; ok && ii < i_end; ++ii) {
+                const ItemGeom g = item_geom(items, ii, seq_lens, bs, cap, flags, false);
+                const int ni = ii - i_begin;
+                if (!(ok = mbar_wait(mb + kBarQFull, ni & 1, flags, abort_flag))) break;
                 tc_fence_after();
-                const uint32_t vreg = sbase + kStageOff + st * kStageBytes + kKRegion;
-                const uint32_t preg = sbase + kPOff + st * kPBytes;
+                if (g.n_tiles > 0) ok = issue_s(gt);
+                if (ok && g.n_tiles > 1) ok = issue_s(gt + 1);
+                for (int j = 0; ok && j < g.n_tiles; ++j) {
+                    const int gj = gt + j, st = gj & 1;
+                    if (!(ok = mbar_wait(mb + kBarPFull + 8 * st, (gj >> 1) & 1, flags, abort_flag)))
+                        break;
+                    if (j == 0 && ni >= 1 &&
+                        !(ok = mbar_wait(mb + kBarOFree, (ni - 1) & 1, flags, abort_flag)))
+                        break;
+                    tc_fence_after();
+                    const uint32_t vreg = sbase + kVOff + st * kVStage;
+                    const uint32_t preg = sbase + kPOff + st * kPBytes;
 #pragma unroll
-                for (int i = 0; i < 2; ++i)
+                    for (int i = 0; i < 2; ++i)
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const uint64_t a = sdesc_sw128(preg + k * 32, 16, 1024);
-                        const uint64_t bd = sdesc_sw128(
-                            vreg + (k >> 1) * 4 * kBox + (k & 1) * 2048 + i * 2 * kBox, kBox, 1024);
-                        mma_pair_f16(tmem + kTmemO + 128 * i, a, bd, id_o,
-                                     (j > 0 || k > 0) ? 1u : 0u);
-                    }
-                mma_commit_pair(bar_odone + 8 * st, 0x3);
-                mma_commit_pair(bar_kempty + 8 * st, 0x3);
-                if (j + 2 < n_tiles) ok = issue_s(j + 2);
+                        for (int k = 0; k < 4; ++k) {
+                            const uint64_t a = sdesc_sw128(preg + k * 32, 16, 1024);
+                            const uint64_t b = sdesc_sw128(
+                                vreg + (k >> 1) * 4 * kBox + (k & 1) * 2048 + i * 2 * kBox, kBox,
+                                1024);
+                            mma_pair_f16(tmem + kTmemO + 128 * i, a, b, id_o,
+                                         (j > 0 || k > 0) ? 1u : 0u);
+                        }
+                    mma_commit_pair(mb + kBarODone + 8 * st, 0x3);
+                    mma_commit_pair(mb + kBarVEmpty + 8 * st, 0x3);
+                    if (j + 2 < g.n_tiles) ok = issue_s(gj + 2);
+                }
+                if (ok) mma_commit_pair(mb + kBarQFree, 0x3);
+                gt += g.n_tiles;
             }
         }
         __syncwarp();
@@ -249,129 +348,148 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
         const int t = tid - 128;            // TMEM lane
         const int hl = t & 63, th = t >> 6; // head within the CTA, token / column half
         const uint32_t lane_base = static_cast<uint32_t>((warp - 4) * 32) << 16;
-        float m_use = -INFINITY, l = 0.f;
+        const uint32_t pfull_leader0 = mapa(mb + kBarPFull, 0);
+        const uint32_t pfull_leader1 = mapa(mb + kBarPFull + 8, 0);
+        const uint32_t ofree_leader = mapa(mb + kBarOFree, 0);
         bool ok = true;
-        // Every softmax warp runs all n_tiles iterations and reaches every
-        // named barrier; after a failed wait it only skips the work.
-        for (int j = 0; j < n_tiles; ++j) {
-            const int st = j & 1;
-            const int vc = min(kTile, t_end - (t_begin + kTile * j));
-            if (ok)
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(bar_sfull + 8 * st, (j >> 1) & 1, flags, abort_flag));
-            float s[32];
-            if (ok) {
-                tc_fence_after();
-                tmem_ld32(tmem + lane_base + 32 * st, s);
-                tmem_wait_ld();
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) s[i] = -INFINITY;
-            }
-            float mx = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                if (th * 32 + i >= vc) s[i] = -INFINITY;
-                mx = fmaxf(mx, s[i]);
-            }
-            red_max[st * 128 + t] = mx;
-            named_sync_softmax();
-            const float mt = fmaxf(mx, red_max[st * 128 + (t ^ 64)]);
-            const float m_new = fmaxf(m_use, mt);
-            const bool resc = m_new > m_use + kTau;
-            float alpha = 1.f;
-            if (resc) {
-                alpha = (m_use == -INFINITY) ? 0.f : exp2f(m_use - m_new);
-                m_use = m_new;
-                l *= alpha;
-            }
-            uint32_t packed[16];
-            float psum = 0.f;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const float p0 = (m_use == -INFINITY) ? 0.f : exp2f(s[2 * i] - m_use);
-                const float p1 = (m_use == -INFINITY) ? 0.f : exp2f(s[2 * i + 1] - m_use);
-                psum += p0 + p1;
-                const __half2 h = __floats2half2_rn(p0, p1);
-                packed[i] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-            l += psum;
-            if (ok && j >= 2)  // P buffer `st` is free once O of tile j-2 completed
-                ok = __all_sync(0xffffffffu, mbar_wait(bar_odone + 8 * st, ((j - 2) >> 1) & 1,
-                                                       flags, abort_flag));
-            if (ok && __any_sync(0xffffffffu, resc && j > 0)) {
-                const int jp = j - 1;  // rescale O accumulated through tile j-1
-                ok = __all_sync(0xffffffffu, mbar_wait(bar_odone + 8 * (jp & 1), (jp >> 1) & 1,
-                                                       flags, abort_flag));
+        int gt = 0;
+        // Every softmax thread runs every iteration and reaches every named
+        // barrier; after a failed wait it only skips the work.
+        for (int ii = i_begin; ii < i_end; ++ii) {
+            const ItemGeom g = item_geom(items, ii, seq_lens, bs, cap, flags, t == 0 && leader);
+            float m_use = -INFINITY, l = 0.f;
+            for (int j = 0; j < g.n_tiles; ++j) {
+                const int gj = gt + j, st = gj & 1;
+                const int vc = min(kTile, g.t_end - (g.t_begin + kTile * j));
+                if (ok)
+                    ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarSFull + 8 * st, (gj >> 1) & 1,
+                                                           flags, abort_flag));
+                float s[32];
                 if (ok) {
                     tc_fence_after();
-#pragma unroll 1
-                    for (int u = 0; u < 8; ++u) {
-                        float o[32];
-                        tmem_ld32(tmem + lane_base + kTmemO + 32 * u, o);
-                        tmem_wait_ld();
+                    tmem_ld32(tmem + lane_base + 32 * st, s);
+                    tmem_wait_ld();
+                } else {
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                        tmem_st32(tmem + lane_base + kTmemO + 32 * u, o);
+                    for (int i = 0; i < 32; ++i) s[i] = -INFINITY;
+                }
+                float mx = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    if (th * 32 + i >= vc) s[i] = -INFINITY;
+                    mx = fmaxf(mx, s[i]);
+                }
+                red_max[st * 128 + t] = mx;
+                named_sync_softmax();
+                const float mt = fmaxf(mx, red_max[st * 128 + (t ^ 64)]);
+                const float m_new = fmaxf(m_use, mt);
+                const bool resc = m_new > m_use + kTau;
+                float alpha = 1.f;
+                if (resc) {
+                    alpha = (m_use == -INFINITY) ? 0.f : fast_exp2(m_use - m_new);
+                    m_use = m_new;
+                    l *= alpha;
+                }
+                const float mneg = (m_use == -INFINITY) ? 0.f : -m_use;
+                uint32_t packed[16];
+                float psum = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float p0 = fast_exp2(s[2 * i] + mneg);
+                    const float p1 = fast_exp2(s[2 * i + 1] + mneg);
+                    psum += p0 + p1;
+                    const __half2 h = __floats2half2_rn(p0, p1);
+                    packed[i] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                l += psum;
+                if (ok && gj >= 2)  // P buffer `st` is free once O of tile gj-2 completed
+                    ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * st,
+                                                           ((gj - 2) >> 1) & 1, flags, abort_flag));
+                if (ok && __any_sync(0xffffffffu, resc && j > 0)) {
+                    const int jp = gj - 1;  // rescale O accumulated through tile gj-1
+                    ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * (jp & 1),
+                                                           (jp >> 1) & 1, flags, abort_flag));
+                    if (ok) {
+                        tc_fence_after();
+#pragma unroll 1
+                        for (int u = 0; u < 8; ++u) {
+                            float o[32];
+                            tmem_ld32(tmem + lane_base + kTmemO + 32 * u, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+                            tmem_st32(tmem + lane_base + kTmemO + 32 * u, o);
+                        }
+                        tmem_wait_st();
                     }
-                    tmem_wait_st();
                 }
-            }
-            if (!ok) continue;
-            uint8_t* prow = smem + kPOff + st * kPBytes + (hl >> 3) * 1024 + (hl & 7) * 128;
+                if (ok) {
+                    uint8_t* prow = smem + kPOff + st * kPBytes + (hl >> 3) * 1024 + (hl & 7) * 128;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t chunk = static_cast<uint32_t>((th * 4 + u) ^ (hl & 7));
-                *reinterpret_cast<uint4*>(prow + chunk * 16) =
-                    make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
-            }
-            if (vc < kTile) {
-                // Rows past the end of the item: zero their value rows so that
-                // p = 0 times whatever the pool holds there stays 0.
-                uint8_t* vreg = smem + kStageOff + st * kStageBytes + kKRegion;
-                const int rows = kTile - vc;
-                for (int idx = t; idx < rows * 4 * 8; idx += 128) {
-                    const int tok = vc + idx / 32, rem = idx % 32, s4 = rem >> 3, c16 = rem & 7;
-                    const int h = tok >> 5, rr = tok & 31;
-                    *reinterpret_cast<uint4*>(vreg + h * 4 * kBox + s4 * kBox + (rr >> 3) * 1024 +
-                                              (rr & 7) * 128 + c16 * 16) = make_uint4(0, 0, 0, 0);
+                    for (int u = 0; u < 4; ++u) {
+                        const uint32_t chunk = static_cast<uint32_t>((th * 4 + u) ^ (hl & 7));
+                        *reinterpret_cast<uint4*>(prow + chunk * 16) = make_uint4(
+                            packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+                    }
+                    // The V tile of this CTA must have landed before O reads it
+                    // (and before rows past the end are cleared).
+                    ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarVFull + 8 * st, (gj >> 1) & 1,
+                                                           flags, abort_flag));
                 }
+                if (ok && vc < kTile) {
+                    // Rows past the end of the item: zero their value rows so
+                    // that p = 0 times whatever the pool holds there stays 0.
+                    uint8_t* vreg = smem + kVOff + st * kVStage;
+                    const int rows = kTile - vc;
+                    for (int idx = t; idx < rows * 32; idx += 128) {
+                        const int tok = vc + idx / 32, rem = idx % 32, s4 = rem >> 3, c16 = rem & 7;
+                        const int h = tok >> 5, rr = tok & 31;
+                        *reinterpret_cast<uint4*>(vreg + h * 4 * kBox + s4 * kBox + (rr >> 3) * 1024 +
+                                                  (rr & 7) * 128 + c16 * 16) = make_uint4(0, 0, 0, 0);
+                    }
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                named_sync_softmax();
+                if (ok && t == 0) mbar_arrive_cluster(st ? pfull_leader1 : pfull_leader0);
             }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(mapa(bar_pfull + 8 * st, 0));
-        }
-        if (ok && n_tiles > 0) {
-            const int jl = n_tiles - 1;
-            ok = __all_sync(0xffffffffu,
-                            mbar_wait(bar_odone + 8 * (jl & 1), (jl >> 1) & 1, flags, abort_flag));
-        }
-        red_sum[t] = l;
-        named_sync_softmax();
-        const float l_tot = l + red_sum[t ^ 64];
-        const int64_t row = (int64_t)item * kHeads + kHeadsPerCta * rank + hl;
-        if (th == 0) {
-            ws.part_m[row] = (ok && m_use != -INFINITY) ? m_use * kLn2 : -INFINITY;
-            ws.part_l[row] = ok ? l_tot : 0.f;
-        }
-        float* dst = ws.part_ctx + row * kValue;
-        const bool have = ok && n_tiles > 0;
-        if (have) tc_fence_after();
+            // Epilogue of the item: partial (m, l, context) of this CTA's heads.
+            if (ok && g.n_tiles > 0) {
+                const int jl = gt + g.n_tiles - 1;
+                ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * (jl & 1), (jl >> 1) & 1,
+                                                       flags, abort_flag));
+            }
+            red_sum[t] = l;
+            named_sync_softmax();
+            const float l_tot = l + red_sum[t ^ 64];
+            const int64_t row = (int64_t)ii * kHeads + kHeadsPerCta * rank + hl;
+            if (th == 0) {
+                ws.part_m[row] = (ok && m_use != -INFINITY) ? m_use * kLn2 : -INFINITY;
+                ws.part_l[row] = ok ? l_tot : 0.f;
+            }
+            float* dst = ws.part_ctx + row * kValue;
+            const bool have = ok && g.n_tiles > 0;
+            if (have) tc_fence_after();
 #pragma unroll 1
-        for (int u = 0; u < 8; ++u) {
-            float o[32];
-            if (have) {
-                tmem_ld32(tmem + lane_base + kTmemO + 32 * u, o);
-                tmem_wait_ld();
-            } else {
+            for (int u = 0; u < 8; ++u) {
+                float o[32];
+                if (have) {
+                    tmem_ld32(tmem + lane_base + kTmemO + 32 * u, o);
+                    tmem_wait_ld();
+                } else {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) o[e] = 0.f;
+                    for (int e = 0; e < 32; ++e) o[e] = 0.f;
+                }
+                const int col = (u >> 2) * 256 + th * 128 + (u & 3) * 32;
+#pragma unroll
+                for (int e = 0; e < 32; e += 4)
+                    *reinterpret_cast<float4*>(dst + col + e) =
+                        make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
             }
-            const int col = (u >> 2) * 256 + th * 128 + (u & 3) * 32;
-#pragma unroll
-            for (int e = 0; e < 32; e += 4)
-                *reinterpret_cast<float4*>(dst + col + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+            tc_fence_before();
+            named_sync_softmax();
+            if (ok && t == 0) mbar_arrive_cluster(ofree_leader);
+            gt += g.n_tiles;
         }
     }
 
@@ -381,6 +499,19 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap tmap, const float* 
     cluster_sync();
     tc_fence_after();
     if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
+}
+
+// q16[b, h, l] = FP16(q_lat[b, h, l] * qscale), the TMA source of Q.
+__global__ void q_prep_kernel(const float4* __restrict__ q, uint2* __restrict__ q16, float qscale,
+                              int64_t n4) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = q[i];
+        const __half2 a = __floats2half2_rn(v.x * qscale, v.y * qscale);
+        const __half2 b = __floats2half2_rn(v.z * qscale, v.w * qscale);
+        q16[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a),
+                            *reinterpret_cast<const uint32_t*>(&b));
+    }
 }
 
 // Flag word used when the caller passes none: a wait that gives up must be
@@ -402,42 +533,58 @@ static bool load_encode() {
     return g_encode != nullptr;
 }
 
+static bool encode_2d_f16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                          uint32_t box_cols, uint32_t box_rows) {
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace tc
 
 bool tc_supported(const plkv_latent_decode_args& a) {
     return a.q_heads == tc::kHeads && a.latent_dim == tc::kLatent && a.value_dim == tc::kValue &&
            a.block_size % 32 == 0 && !a.scores && !a.probs &&
            a.num_physical * (int64_t)a.block_size < (1ll << 31) &&
+           (int64_t)a.batch * tc::kHeads < (1ll << 31) &&
            (reinterpret_cast<uintptr_t>(a.cache) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(a.q_lat) & 15) == 0;
 }
 
 cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWorkspace ws,
                                      cudaStream_t st) {
-    if (!tc::load_encode()) return cudaErrorNotSupported;
-    CUtensorMap map;
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.latent_dim),
-                          static_cast<cuuint64_t>(a.num_physical) * a.block_size};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(a.latent_dim) * 2};
-    cuuint32_t box[2] = {64, 32};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = tc::g_encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                              const_cast<uint16_t*>(a.cache), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(tc::latent_partial_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)tc::kSmemBytes);
+    if (!tc::load_encode() || !ws.q16) return cudaErrorNotSupported;
+    CUtensorMap cache_map, q_map;
+    if (!tc::encode_2d_f16(&cache_map, a.cache, tc::kLatent,
+                           static_cast<uint64_t>(a.num_physical) * a.block_size, 64, 32) ||
+        !tc::encode_2d_f16(&q_map, ws.q16, tc::kLatent, static_cast<uint64_t>(a.batch) * tc::kHeads,
+                           64, 64))
+        return cudaErrorInvalidValue;
+    const int64_t n4 = (int64_t)a.batch * tc::kHeads * tc::kLatent / 4;
+    int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
+    tc::q_prep_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const float4*>(a.q_lat),
+                                              reinterpret_cast<uint2*>(ws.q16),
+                                              a.scale * 1.4426950408889634f, n4);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(tc::latent_partial_tc_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
     if (e != cudaSuccess) return e;
     int32_t* flags = a.err_flags;
     if (!flags) {
         e = cudaGetSymbolAddress(reinterpret_cast<void**>(&flags), tc::g_tc_flags);
         if (e != cudaSuccess) return e;
     }
-    tc::latent_partial_tc_kernel<<<2 * a.n_items, 256, tc::kSmemBytes, st>>>(
-        map, a.q_lat, a.scale * 1.4426950408889634f, a.block_size, a.block_tables, a.max_blocks,
-        a.num_physical, a.seq_lens, a.items, ws, flags);
+    const int workers = (a.worker_item_begin && a.n_workers > 0) ? a.n_workers : a.n_items;
+    tc::latent_partial_tc_kernel<<<2 * workers, 256, tc::kSmemBytes, st>>>(
+        cache_map, q_map, a.block_size, a.block_tables, a.max_blocks, a.num_physical, a.seq_lens,
+        a.items, (a.worker_item_begin && a.n_workers > 0) ? a.worker_item_begin : nullptr, ws,
+        flags);
     return cudaGetLastError();
 }
 

@@ -49,7 +49,8 @@ extern "C" int plkv_latent_decode_noalloc(const plkv_latent_decode_args* args,
     if (args->n_items <= 0 || args->batch <= 0 || args->q_heads <= 0 || args->value_dim <= 0)
         return PLKV_ERR_ZERO_VALUE;
     const size_t need =
-        plkv::decode_workspace_bytes(args->n_items, args->batch, args->q_heads, args->value_dim);
+        plkv::decode_workspace_bytes(args->n_items, args->batch, args->q_heads, args->latent_dim,
+                                     args->value_dim);
     if (need > (size_t)PLKV_NOALLOC_SCRATCH_BYTES) return PLKV_ERR_WORKSPACE;
     void* scratch = nullptr;
     int st = scratch_address(&scratch);

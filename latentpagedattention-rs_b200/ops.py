@@ -227,7 +227,7 @@ def paged_latent_write_fp16_storage(latent_cache: torch.Tensor, block_table, tok
 
 @dataclass
 class DecodePlan:
-    """Split-K work items on the device (from plkv_plan_splits)."""
+    """Split-K work items on the device (from plkv_plan_splits / plkv_plan_workers)."""
 
     items: torch.Tensor           # [n_items, 4] int32 (seq, block_begin, block_end, 0)
     seq_item_begin: torch.Tensor  # [batch + 1] int32
@@ -235,6 +235,8 @@ class DecodePlan:
     batch: int
     items_host: np.ndarray
     seq_item_begin_host: np.ndarray
+    worker_item_begin: torch.Tensor | None = None  # [n_workers + 1] int32
+    n_workers: int = 0
 
 
 def default_target_items(device: torch.device | None = None) -> int:
@@ -268,6 +270,34 @@ def plan_splits(seq_lens_host, block_size: int, *, target_items: int | None = No
                       n.value, batch, items, begin)
 
 
+def plan_workers(seq_lens_host, block_size: int, *, n_workers: int | None = None,
+                 device: torch.device | str = "cuda") -> DecodePlan:
+    """Balanced plan for the persistent tensor-core decode: the blocks of all
+    sequences are cut into `n_workers` equal contiguous ranges (default: one
+    per CTA pair of the device)."""
+    lens = np.ascontiguousarray(np.asarray(seq_lens_host, dtype=np.int32))
+    batch = int(lens.size)
+    device = torch.device(device)
+    if n_workers is None:
+        n_workers = default_target_items(device if device.type == "cuda" else None) // 4
+    n = ctypes.c_int32(0)
+    L = lib()
+    st = L.plkv_plan_workers(lens.ctypes.data, batch, block_size, n_workers, None, 0, None, None,
+                             ctypes.byref(n))
+    if st not in (_lib.PLKV_OK, _lib.PLKV_ERR_WORKSPACE):
+        check(st, "plkv_plan_workers")
+    items = np.zeros((max(n.value, 1), 4), dtype=np.int32)
+    begin = np.zeros(batch + 1, dtype=np.int32)
+    wbegin = np.zeros(n_workers + 1, dtype=np.int32)
+    check(L.plkv_plan_workers(lens.ctypes.data, batch, block_size, n_workers, items.ctypes.data,
+                              n.value, begin.ctypes.data, wbegin.ctypes.data, ctypes.byref(n)),
+          "plkv_plan_workers")
+    items = items[:n.value]
+    return DecodePlan(torch.as_tensor(items, device=device), torch.as_tensor(begin, device=device),
+                      n.value, batch, items, begin, torch.as_tensor(wbegin, device=device),
+                      n_workers)
+
+
 # ------------------------------------------------------------------- decode
 
 def project_query(q: torch.Tensor, w_k_head_major: torch.Tensor) -> torch.Tensor:
@@ -284,8 +314,10 @@ def project_query(q: torch.Tensor, w_k_head_major: torch.Tensor) -> torch.Tensor
     return q_lat
 
 
-def latent_workspace_bytes(n_items: int, batch: int, q_heads: int, value_dim: int) -> int:
-    return int(lib().plkv_latent_decode_workspace_size(n_items, batch, q_heads, value_dim))
+def latent_workspace_bytes(n_items: int, batch: int, q_heads: int, latent_dim: int,
+                           value_dim: int) -> int:
+    return int(lib().plkv_latent_decode_workspace_size(n_items, batch, q_heads, latent_dim,
+                                                       value_dim))
 
 
 def latent_decode(q_lat: torch.Tensor, cache: torch.Tensor, block_tables: torch.Tensor,
@@ -331,7 +363,7 @@ def latent_decode(q_lat: torch.Tensor, cache: torch.Tensor, block_tables: torch.
     scores = (torch.empty((B, Hq, max_seq_len), dtype=torch.float32, device=dev)
               if (want_scores or want_probs) else None)
     probs = torch.empty_like(scores) if want_probs else None
-    need = latent_workspace_bytes(plan.n_items, B, Hq, Lv)
+    need = latent_workspace_bytes(plan.n_items, B, Hq, L, Lv)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=dev)
     a = _lib.LatentDecodeArgs(
@@ -339,6 +371,7 @@ def latent_decode(q_lat: torch.Tensor, cache: torch.Tensor, block_tables: torch.
         value_dim=Lv, batch=B, q_heads=Hq, scale=float(scale), block_tables=_ptr(block_tables),
         max_blocks=block_tables.shape[1], seq_lens=_ptr(seq_lens), items=_ptr(plan.items),
         seq_item_begin=_ptr(plan.seq_item_begin), n_items=plan.n_items,
+        worker_item_begin=_ptr(plan.worker_item_begin), n_workers=plan.n_workers,
         allow_empty=int(allow_empty), w_v=_ptr(w_v), proj_heads=PH, head_dim=D, ctx=_ptr(out),
         lse=_ptr(lse), scores=_ptr(scores), probs=_ptr(probs),
         max_seq_len=int(max_seq_len or 0),

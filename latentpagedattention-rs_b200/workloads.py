@@ -186,13 +186,12 @@ def device_inputs(s: WorkloadSpec, device, *, shards: int = 1, shard: int = 0,
     if s.out_dim and with_out_proj:
         out["w_o"] = torch.randn((Hq * D, s.out_dim), generator=gw, device=dev) / math.sqrt(Hq * D)
     out["new_rows"] = torch.randn((s.batch, L), generator=gw, device=dev) * s.cache_std
-    nblk_global = (lens.astype(np.int64) + s.steps - 1 + s.block_size - 1) // s.block_size
     if shards > 1:
-        lo = first_block * s.block_size
-        hi = np.minimum(((nblk_global * (shard + 1)) // shards) * s.block_size, lens)
-        local = np.clip(hi - lo, 0, None).astype(np.int32)
+        from .multigpu import split_k_ranges
+
+        _, _, local = split_k_ranges(lens, s.block_size, shards, shard, s.steps - 1)
         out["lens"] = local
-        out["token_offset"] = lo
+        out["token_offset"] = first_block * s.block_size
     else:
         out["lens"] = lens.copy()
         out["token_offset"] = np.zeros(s.batch, dtype=np.int64)

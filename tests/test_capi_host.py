@@ -120,7 +120,7 @@ def test_host_validation_before_launch():
     assert L.plkv_fullkv_decode(ctypes.byref(f), None) == m.PLKV_ERR_INVALID_PAGED_LOOKUP
     assert L.plkv_out_proj(fake, fake, fake, 65, 16, 16, 1, fake, 1 << 20, None) == \
         m.PLKV_ERR_UNSUPPORTED
-    assert L.plkv_latent_decode_workspace_size(10, 2, 4, 8) > 10 * 4 * 8 * 4
+    assert L.plkv_latent_decode_workspace_size(10, 2, 4, 8, 8) > 10 * 4 * 8 * 4
 
 
 def test_product_never_imports_the_oracle():
@@ -131,3 +131,39 @@ def test_product_never_imports_the_oracle():
                 text = open(os.path.join(dirpath, f), encoding="utf-8").read()
                 assert "import oracle" not in text and "from oracle" not in text, f
                 assert "plkv_oracle" not in text, f
+
+
+def _plan_workers(lens, bs, workers):
+    m = _lib_mod()
+    lens = np.ascontiguousarray(np.asarray(lens, np.int32))
+    n = ctypes.c_int32(0)
+    st = m.lib().plkv_plan_workers(lens.ctypes.data, lens.size, bs, workers, None, 0, None, None,
+                                   ctypes.byref(n))
+    assert st == m.PLKV_ERR_WORKSPACE
+    items = np.zeros((n.value, 4), np.int32)
+    begin = np.zeros(lens.size + 1, np.int32)
+    wbegin = np.zeros(workers + 1, np.int32)
+    st = m.lib().plkv_plan_workers(lens.ctypes.data, lens.size, bs, workers, items.ctypes.data,
+                                   n.value, begin.ctypes.data, wbegin.ctypes.data, ctypes.byref(n))
+    assert st == m.PLKV_OK
+    return items, begin, wbegin
+
+
+@pytest.mark.parametrize("lens,bs,workers", [
+    ([131072] * 8, 64, 74), ([7, 13], 4, 74), ([0, 5000, 0, 3], 64, 3), ([1], 64, 1),
+    (list(np.random.default_rng(3).integers(1024, 32769, 64)), 64, 74), ([640] * 3, 64, 40)])
+def test_worker_plan_balances_and_covers(lens, bs, workers):
+    items, begin, wbegin = _plan_workers(lens, bs, workers)
+    assert begin[0] == 0 and begin[-1] == len(items)
+    assert wbegin[0] == 0 and wbegin[-1] == len(items) and np.all(np.diff(wbegin) >= 0)
+    for b, n in enumerate(lens):
+        its = items[begin[b]:begin[b + 1]]
+        assert len(its) >= 1 and np.all(its[:, 0] == b)
+        nb = (n + bs - 1) // bs
+        covered = np.concatenate([np.arange(i[1], i[2]) for i in its])
+        np.testing.assert_array_equal(covered, np.arange(nb))
+    total = sum((n + bs - 1) // bs for n in lens)
+    per_worker = [int(np.sum(items[wbegin[w]:wbegin[w + 1], 2] - items[wbegin[w]:wbegin[w + 1], 1]))
+                  for w in range(workers)]
+    assert sum(per_worker) == total
+    assert max(per_worker) - min(per_worker) <= 1

@@ -322,9 +322,10 @@ def _mla_case(pkg, batch, lens, seed=5):
                 bs=bs, L=L, Lv=Lv, Hq=Hq, D=D, scale=1 / math.sqrt(D))
 
 
-def _check_mla(ops, m, mode, rel, heads=(0, 37, 127), target=None, lse_tol=1e-4):
+def _check_mla(ops, m, mode, rel, heads=(0, 37, 127), target=None, lse_tol=1e-4, workers=None):
     lens_host = m["lens"]
-    plan = ops.plan_splits(lens_host, m["bs"], target_items=target)
+    plan = (ops.plan_workers(lens_host, m["bs"], n_workers=workers) if workers
+            else ops.plan_splits(lens_host, m["bs"], target_items=target))
     r = ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]), t(lens_host), plan,
                           scale=m["scale"], value_dim=m["Lv"], w_v=t(m["w_uv"]), mode=mode,
                           want_lse=True)
@@ -365,18 +366,27 @@ def test_mla_tensor_core_small_batch(ops, pkg, lens):
     assert int(flags.item()) == 0
     _check_mla(ops, m, "tc", TC_REL, heads=(0, 63, 64, 127), lse_tol=2e-3)
     _check_mla(ops, m, "tc", TC_REL, heads=(5, 100), target=3, lse_tol=2e-3)
+    # Persistent CTA pairs: several items per worker, items crossing sequences.
+    _check_mla(ops, m, "tc", TC_REL, heads=(1, 66), lse_tol=2e-3, workers=2)
+    _check_mla(ops, m, "tc", TC_REL, heads=(2, 127), lse_tol=2e-3, workers=5)
 
 
-def test_tensor_core_matches_exact_mode(ops, pkg):
-    m = _mla_case(pkg, 4, [900, 2048, 131, 6000], seed=13)
+@pytest.mark.parametrize("workers", [0, 1, 7, 74])
+def test_tensor_core_matches_exact_mode(ops, pkg, workers):
+    m = _mla_case(pkg, 5, [900, 2048, 0, 131, 6000], seed=13)
     outs = {}
     for mode in ("exact", "tc"):
-        plan = ops.plan_splits(m["lens"], m["bs"])
+        plan = (ops.plan_workers(m["lens"], m["bs"], n_workers=workers) if mode == "tc" and workers
+                else ops.plan_splits(m["lens"], m["bs"]))
         outs[mode] = ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]),
                                        t(m["lens"]), plan, scale=m["scale"], value_dim=m["Lv"],
-                                       w_v=t(m["w_uv"]), mode=mode, want_lse=True)
+                                       w_v=t(m["w_uv"]), mode=mode, want_lse=True,
+                                       allow_empty=True)
     assert rel_err(outs["tc"]["ctx"].cpu(), outs["exact"]["ctx"].cpu()) <= TC_REL
-    assert rel_err(outs["tc"]["lse"].cpu(), outs["exact"]["lse"].cpu()) <= TC_REL
+    le, lt = outs["exact"]["lse"].cpu(), outs["tc"]["lse"].cpu()
+    fin = torch.isfinite(le)
+    assert torch.equal(fin, torch.isfinite(lt))
+    assert rel_err(lt[fin], le[fin]) <= TC_REL
 
 
 def test_tensor_core_rejects_intermediates(ops, pkg):
@@ -465,7 +475,8 @@ def test_long_context_tensor_core_full_size(ops, pkg):
     lens = t(x["lens"])
     res = {}
     for mode in ("exact", "tc"):
-        plan = ops.plan_splits(x["lens"], s.block_size)
+        plan = (ops.plan_workers(x["lens"], s.block_size) if mode == "tc"
+                else ops.plan_splits(x["lens"], s.block_size))
         res[mode] = ops.latent_decode(x["q_lat"], x["cache"], x["tables"], lens, plan,
                                       scale=s.scale, value_dim=s.value_dim, w_v=x["w_v"],
                                       mode=mode)["ctx"].cpu()

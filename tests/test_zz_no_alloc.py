@@ -72,8 +72,8 @@ def _run_both(ops, _lib, c, target_items):
     stream = torch.cuda.current_stream().cuda_stream
     ref_ctx = torch.empty((B, Hq, D), dtype=torch.float32, device="cuda")
     ref_lse = torch.empty((B, Hq), dtype=torch.float32, device="cuda")
-    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, B, Hq, c["Lv"]), dtype=torch.uint8,
-                     device="cuda")
+    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, B, Hq, c["L"], c["Lv"]),
+                     dtype=torch.uint8, device="cuda")
     a = _args(_lib, c, plan, ref_ctx, ref_lse, ws)
     assert L.plkv_latent_decode(ctypes.byref(a), stream) == _lib.PLKV_OK
     ctx = torch.full((B, Hq, D), float("nan"), dtype=torch.float32, device="cuda")
@@ -89,7 +89,7 @@ def test_noalloc_decode_matches_workspace_decode_twice():
     _lib = importlib.import_module(PACKAGE + "._lib")
     first = _case(21, [4000, 37, 1500])
     ctx, lse, ref_ctx, ref_lse, plan = _run_both(ops, _lib, first, target_items=40)
-    assert ops.latent_workspace_bytes(plan.n_items, 3, 128, 512) <= SCRATCH_LIMIT
+    assert ops.latent_workspace_bytes(plan.n_items, 3, 128, 576, 512) <= SCRATCH_LIMIT
     assert torch.isfinite(ctx).all()
     assert rel_err(ctx, ref_ctx) <= EXACT_REL
     assert rel_err(lse, ref_lse) <= EXACT_REL
@@ -107,7 +107,7 @@ def test_noalloc_rejects_requests_beyond_the_scratch_array():
     _lib = importlib.import_module(PACKAGE + "._lib")
     c = _case(23, [64 * 200])
     plan = ops.plan_splits(c["lens_host"], c["bs"], target_items=200)
-    assert ops.latent_workspace_bytes(plan.n_items, 1, 128, 512) > SCRATCH_LIMIT
+    assert ops.latent_workspace_bytes(plan.n_items, 1, 128, 576, 512) > SCRATCH_LIMIT
     ctx = torch.zeros((1, 128, 128), dtype=torch.float32, device="cuda")
     lse = torch.zeros((1, 128), dtype=torch.float32, device="cuda")
     a = _args(_lib, c, plan, ctx, lse, None)
