@@ -8,59 +8,70 @@
 
 namespace plkv {
 
-constexpr int kCombineRows = 8;  // (sequence, head) rows per CTA
+constexpr int kCombineRows = 8;   // (sequence, head) rows per CTA
+constexpr int kMaxWidthPerLane = 20;  // width <= 640
+constexpr int kLSlices = 8;       // latent-row slices of the projection
 
 // grid = (proj_heads, ceil(batch * group / kCombineRows)), block = 256.
 // Row r of the CTA is (b, h) with h = p * group + (gr % group), b = gr / group.
-// Phase 1: warp per row merges the row's items:
-//   M = max_i m_i,  S = sum_i l_i exp(m_i - M),
+// Phase 1: warp per row merges the row's items in registers (lane owns
+//   columns lane + 32k):  M = max_i m_i,  S = sum_i l_i exp(m_i - M),
 //   c[col] = sum_i ctx_i[col] exp(m_i - M) / S.
-// Phase 2: out[d] = sum_l c[l] * W[p, l, d] in increasing l (lib.rs:1066-1071),
-// or c itself when there is no projection.
+// Phase 2: out[d] = sum_l c[l] * W[p, l, d] (lib.rs:1066-1071).  With
+//   d % 4 == 0 and D <= 128 the 256 threads are (latent slice s) x (group of
+//   4 columns): each thread sums its slice of l with float4 weight loads, then
+//   the slices are added in a fixed order; otherwise a column per thread.
+// Without a projection, c itself is written.
 __global__ void __launch_bounds__(256)
 combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_begin, int B,
                        int Hq, int width, const float* __restrict__ w, int proj_heads, int D,
                        float* __restrict__ out, float* __restrict__ lse) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    float* cs = reinterpret_cast<float*>(smem_raw);  // [kCombineRows][width]
+    float* cs = reinterpret_cast<float*>(smem_raw);           // [kCombineRows][width]
+    float* red = cs + kCombineRows * width;                   // [kLSlices][kCombineRows][128]
     const int group = Hq / proj_heads;
     const int p = blockIdx.x;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rows_total = B * group;
     const int r0 = blockIdx.y * kCombineRows;
     const int nrows = min(kCombineRows, rows_total - r0);
+    const int ncol = (width + 31) / 32;
 
     for (int r = warp; r < kCombineRows; r += 8) {
-        float* c = cs + r * width;
-        if (r >= nrows) {
-            for (int col = lane; col < width; col += 32) c[col] = 0.f;
-            continue;
-        }
-        const int gr = r0 + r;
-        const int b = gr / group, h = p * group + gr % group;
-        const int ib = seq_item_begin[b], ie = seq_item_begin[b + 1];
-        float M = -INFINITY;
-        for (int i = ib + lane; i < ie; i += 32) M = fmaxf(M, ws.part_m[(int64_t)i * Hq + h]);
-        M = warp_max(M);
-        float S = 0.f;
-        for (int i = ib + lane; i < ie; i += 32) {
-            const float mi = ws.part_m[(int64_t)i * Hq + h];
-            if (mi != -INFINITY) S += ws.part_l[(int64_t)i * Hq + h] * expf(mi - M);
-        }
-        S = warp_sum(S);
-        for (int col = lane; col < width; col += 32) c[col] = 0.f;
-        if (M != -INFINITY) {
-            for (int i = ib; i < ie; ++i) {
-                const float mi = ws.part_m[(int64_t)i * Hq + h];
-                if (mi == -INFINITY) continue;
-                const float wi = expf(mi - M);
-                const float* src = ws.part_ctx + ((int64_t)i * Hq + h) * width;
-                for (int col = lane; col < width; col += 32) c[col] = fmaf(src[col], wi, c[col]);
+        float acc[kMaxWidthPerLane];
+#pragma unroll
+        for (int k = 0; k < kMaxWidthPerLane; ++k) acc[k] = 0.f;
+        float M = -INFINITY, S = 0.f;
+        int b = 0, h = 0;
+        if (r < nrows) {
+            const int gr = r0 + r;
+            b = gr / group;
+            h = p * group + gr % group;
+            const int ib = seq_item_begin[b], ie = seq_item_begin[b + 1];
+            for (int i = ib + lane; i < ie; i += 32) M = fmaxf(M, ws.part_m[(int64_t)i * Hq + h]);
+            M = warp_max(M);
+            if (M != -INFINITY) {
+                for (int i = ib; i < ie; ++i) {
+                    const float mi = ws.part_m[(int64_t)i * Hq + h];
+                    if (mi == -INFINITY) continue;
+                    const float wi = expf(mi - M);
+                    S += ws.part_l[(int64_t)i * Hq + h] * wi;
+                    const float* src = ws.part_ctx + ((int64_t)i * Hq + h) * width;
+#pragma unroll
+                    for (int k = 0; k < kMaxWidthPerLane; ++k) {
+                        const int col = lane + 32 * k;
+                        if (k < ncol && col < width) acc[k] = fmaf(src[col], wi, acc[k]);
+                    }
+                }
             }
-            const float inv = 1.f / S;
-            for (int col = lane; col < width; col += 32) c[col] *= inv;
         }
-        if (lane == 0) {
+        const float inv = (M != -INFINITY) ? 1.f / S : 0.f;
+#pragma unroll
+        for (int k = 0; k < kMaxWidthPerLane; ++k) {
+            const int col = lane + 32 * k;
+            if (k < ncol && col < width) cs[r * width + col] = acc[k] * inv;
+        }
+        if (r < nrows && lane == 0) {
             ws.row_m[(int64_t)b * Hq + h] = M;
             ws.row_l[(int64_t)b * Hq + h] = S;
             if (lse) lse[(int64_t)b * Hq + h] = (M == -INFINITY) ? -INFINITY : M + logf(S);
@@ -78,24 +89,56 @@ combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_
         return;
     }
     const float* wp = w + (int64_t)p * width * D;
+    if ((D & 3) == 0 && D <= 128) {
+        const int dg = tid & 31, slice = tid >> 5;
+        const int l0 = (width * slice) / kLSlices, l1 = (width * (slice + 1)) / kLSlices;
+        float acc[kCombineRows][4];
+#pragma unroll
+        for (int r = 0; r < kCombineRows; ++r)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
+        if (4 * dg < D) {
+#pragma unroll 4
+            for (int l = l0; l < l1; ++l) {
+                const float4 wv = __ldg(reinterpret_cast<const float4*>(wp + (int64_t)l * D) + dg);
+#pragma unroll
+                for (int r = 0; r < kCombineRows; ++r) {
+                    const float c = cs[r * width + l];
+                    acc[r][0] = fmaf(c, wv.x, acc[r][0]);
+                    acc[r][1] = fmaf(c, wv.y, acc[r][1]);
+                    acc[r][2] = fmaf(c, wv.z, acc[r][2]);
+                    acc[r][3] = fmaf(c, wv.w, acc[r][3]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kCombineRows; ++r)
+                *reinterpret_cast<float4*>(red + (slice * kCombineRows + r) * 128 + 4 * dg) =
+                    make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        }
+        __syncthreads();
+        for (int i = tid; i < nrows * D; i += 256) {
+            const int r = i / D, d = i - r * D;
+            float v = 0.f;
+#pragma unroll
+            for (int sl = 0; sl < kLSlices; ++sl) v += red[(sl * kCombineRows + r) * 128 + d];
+            const int gr = r0 + r;
+            const int b = gr / group, h = p * group + gr % group;
+            out[((int64_t)b * Hq + h) * D + d] = v;
+        }
+        return;
+    }
     for (int d0 = 0; d0 < D; d0 += 256) {
-        // Threads split as (row set) x (column d): tpr threads per row set.
-        const int dcount = min(256, D - d0);
-        const int sets = 256 / dcount;
-        const int set = tid / dcount, d = d0 + tid % dcount;
-        if (set >= sets) continue;
+        const int d = d0 + tid;
+        if (d >= D) continue;
         float acc[kCombineRows];
 #pragma unroll
         for (int r = 0; r < kCombineRows; ++r) acc[r] = 0.f;
         for (int l = 0; l < width; ++l) {
             const float wv = wp[(int64_t)l * D + d];
 #pragma unroll
-            for (int r = 0; r < kCombineRows; ++r)
-                if (r % sets == set) acc[r] = fmaf(cs[r * width + l], wv, acc[r]);
+            for (int r = 0; r < kCombineRows; ++r) acc[r] = fmaf(cs[r * width + l], wv, acc[r]);
         }
-#pragma unroll
-        for (int r = 0; r < kCombineRows; ++r) {
-            if (r % sets != set || r >= nrows) continue;
+        for (int r = 0; r < nrows; ++r) {
             const int gr = r0 + r;
             const int b = gr / group, h = p * group + gr % group;
             out[((int64_t)b * Hq + h) * D + d] = acc[r];
@@ -107,13 +150,12 @@ cudaError_t launch_combine(DecodeWorkspace ws, const int32_t* seq_item_begin, in
                            int width, const float* w, int proj_heads, int D, float* out,
                            float* lse, cudaStream_t st) {
     if (!w) proj_heads = Hq;
+    if (width > 32 * kMaxWidthPerLane) return cudaErrorInvalidValue;
     const int group = Hq / proj_heads;
-    const size_t smem = size_t(kCombineRows) * width * 4;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(combine_project_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
+    const size_t smem = size_t(kCombineRows) * width * 4 + size_t(kLSlices) * kCombineRows * 128 * 4;
+    cudaError_t e = cudaFuncSetAttribute(combine_project_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
     dim3 grid(proj_heads, (B * group + kCombineRows - 1) / kCombineRows);
     combine_project_kernel<<<grid, 256, smem, st>>>(ws, seq_item_begin, B, Hq, width, w,
                                                      proj_heads, D, out, lse);

@@ -74,6 +74,7 @@ constexpr uint32_t kVTx = kVStage;                            // own CTA
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 64;                               // S buffers at 0 and 32
 constexpr float kTau = 8.f;
+constexpr int kPrefetchTiles = 6;                             // L2 prefetch distance
 constexpr float kLn2 = 0.6931471805599453f;
 
 // Misc region: barriers (8 bytes each), then small shared arrays.
@@ -155,7 +156,8 @@ __device__ __forceinline__ int half_row(const ItemGeom& g, int j, int h,
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
 latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
-                         const __grid_constant__ CUtensorMap q_map, int bs,
+                         const __grid_constant__ CUtensorMap q_map,
+                         const uint16_t* __restrict__ cache, int bs,
                          const int32_t* __restrict__ tables, int64_t max_blocks,
                          int64_t num_physical, const int32_t* __restrict__ seq_lens,
                          const plkv_work_item* __restrict__ items,
@@ -236,7 +238,19 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                 // The first K tiles of an item only need free K stages; Q waits
                 // for every MMA of the previous item, so load it after them.
                 const int pre = min(2, g.n_tiles);
+                // L2 prefetch of this CTA's token half of the item's first tiles;
+                // then kPrefetchTiles ahead of the K loads.  The peer prefetches
+                // the other half, so both halves of every tile reach L2 early.
+                for (int j = 0; j < min(kPrefetchTiles, g.n_tiles); ++j)
+                    prefetch_l2(cache + (int64_t)half_row(g, j, (int)rank, tables, max_blocks,
+                                                          num_physical, bs, flags) * kLatent,
+                                32 * kLatent * 2);
                 for (int j = 0; ok && j < g.n_tiles; ++j) {
+                    if (j + kPrefetchTiles < g.n_tiles)
+                        prefetch_l2(cache + (int64_t)half_row(g, j + kPrefetchTiles, (int)rank,
+                                                              tables, max_blocks, num_physical, bs,
+                                                              flags) * kLatent,
+                                    32 * kLatent * 2);
                     if (j == pre && !(ok = load_q())) break;
                     const int gj = gt + j, st = gj & 1;
                     if (gj >= 2 && !(ok = mbar_wait(mb + kBarKEmpty + 8 * st, ((gj - 2) >> 1) & 1,
@@ -582,7 +596,8 @@ cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWor
     }
     const int workers = (a.worker_item_begin && a.n_workers > 0) ? a.n_workers : a.n_items;
     tc::latent_partial_tc_kernel<<<2 * workers, 256, tc::kSmemBytes, st>>>(
-        cache_map, q_map, a.block_size, a.block_tables, a.max_blocks, a.num_physical, a.seq_lens,
+        cache_map, q_map, a.cache, a.block_size, a.block_tables, a.max_blocks, a.num_physical,
+        a.seq_lens,
         a.items, (a.worker_item_begin && a.n_workers > 0) ? a.worker_item_begin : nullptr, ws,
         flags);
     return cudaGetLastError();

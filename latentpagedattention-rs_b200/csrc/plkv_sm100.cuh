@@ -123,6 +123,13 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     return p;
 }
 
+// Bulk prefetch of a contiguous global range into L2 (16-byte aligned, size a
+// multiple of 16); no shared memory is used.
+__device__ __forceinline__ void prefetch_l2(const void* ptr, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                 ::"l"(reinterpret_cast<uint64_t>(ptr)), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
