@@ -98,7 +98,7 @@ combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
         if (4 * dg < D) {
-#pragma unroll 4
+#pragma unroll 16
             for (int l = l0; l < l1; ++l) {
                 const float4 wv = __ldg(reinterpret_cast<const float4*>(wp + (int64_t)l * D) + dg);
 #pragma unroll

@@ -72,7 +72,8 @@ constexpr uint32_t kQTx = 2u * kQBytes;                       // both CTAs
 constexpr uint32_t kKTx = 2u * kKStage;                       // both CTAs
 constexpr uint32_t kVTx = kVStage;                            // own CTA
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemO = 64;                               // S buffers at 0 and 32
+constexpr int kSBufs = 4;                                     // S accumulators in TMEM
+constexpr uint32_t kTmemO = 32 * kSBufs;                      // S buffers at 0, 32, 64, 96
 constexpr float kTau = 8.f;
 constexpr int kPrefetchTiles = 6;                             // L2 prefetch distance
 constexpr float kLn2 = 0.6931471805599453f;
@@ -85,12 +86,12 @@ enum : uint32_t {
     kBarKEmpty = 32,   // [2] both: S of the tile completed
     kBarVFull = 48,    // [2] own: V tile landed in this CTA
     kBarVEmpty = 64,   // [2] both: O of the tile completed (V reusable)
-    kBarSFull = 80,    // [2] both: S of the tile in TMEM
-    kBarPFull = 96,    // [2] leader: P written (and V checked) in both CTAs
-    kBarODone = 112,   // [2] both: O of the tile completed (P buffer reusable)
-    kBarOFree = 128,   // leader: epilogue of the item read O in both CTAs
-    kTmemSlot = 136,
-    kAbort = 140,
+    kBarPFull = 80,    // [2] leader: P written (and V checked) in both CTAs
+    kBarODone = 96,    // [2] both: O of the tile completed (P buffer reusable)
+    kBarOFree = 112,   // leader: epilogue of the item read O in both CTAs
+    kBarSFull = 120,   // [kSBufs] both: S of the tile in TMEM
+    kTmemSlot = 152,
+    kAbort = 156,
     kRedMax = 256,     // [2][128] float
     kRedSum = 256 + 1024,
 };
@@ -193,10 +194,10 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
             mbar_init(mb + kBarKEmpty + 8 * i, 1);
             mbar_init(mb + kBarVFull + 8 * i, 1);
             mbar_init(mb + kBarVEmpty + 8 * i, 1);
-            mbar_init(mb + kBarSFull + 8 * i, 1);
             mbar_init(mb + kBarPFull + 8 * i, 2);
             mbar_init(mb + kBarODone + 8 * i, 1);
         }
+        for (int i = 0; i < kSBufs; ++i) mbar_init(mb + kBarSFull + 8 * i, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -298,43 +299,69 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
         __syncwarp();
     } else if (warp == 1) {
         // ---------------------------------------------- MMA issue (leader)
+        // One thread schedules both MMAs without blocking: S(g) as soon as K
+        // tile g landed and one of the kSBufs S accumulators is free (its
+        // previous tile's O was issued, so its softmax is done), O(g) as soon
+        // as P(g) is ready.  S work thus stays queued on the tensor pipe while
+        // the softmax of earlier tiles runs.  S never crosses into the next
+        // item before that item's Q is loaded, which waits for every MMA of
+        // the current item (barrier QFree).
         if (leader && lane == 0) {
             const uint32_t id_s = idesc_f16(128, 64, false, false);
             const uint32_t id_o = idesc_f16(128, 256, false, true);
-            auto issue_s = [&](int gs) -> bool {
-                const int st = gs & 1;
-                if (!mbar_wait(mb + kBarKFull + 8 * st, (gs >> 1) & 1, flags, abort_flag))
-                    return false;
-                tc_fence_after();
-                const uint32_t kreg = sbase + kKOff + st * kKStage;
+            const int n_items_w = i_end - i_begin;
+            int si = 0, sj = 0, sg = 0;  // S cursor: item, tile in item, global tile
+            int oi = 0, oj = 0, og = 0;  // O cursor
+            bool s_q = false;            // Q of item si waited for
+            ItemGeom gs = n_items_w > 0 ? item_geom(items, i_begin, seq_lens, bs, cap, flags, false)
+                                        : ItemGeom{0, 0, 0, 0};
+            ItemGeom go = gs;
+            uint64_t idle_since = 0;
+            while (oi < n_items_w) {
+                bool did = false;
+                if (si < n_items_w) {
+                    if (!s_q && mbar_try_wait(mb + kBarQFull, si & 1)) {
+                        s_q = true;
+                        tc_fence_after();
+                    }
+                    if (s_q) {
+                        if (sj >= gs.n_tiles) {
+                            if (++si < n_items_w)
+                                gs = item_geom(items, i_begin + si, seq_lens, bs, cap, flags, false);
+                            sj = 0;
+                            s_q = false;
+                            did = true;
+                        } else if (sg < og + kSBufs &&
+                                   mbar_try_wait(mb + kBarKFull + 8 * (sg & 1), (sg >> 1) & 1)) {
+                            tc_fence_after();
+                            const int st = sg & 1, sb = sg % kSBufs;
+                            const uint32_t kreg = sbase + kKOff + st * kKStage;
 #pragma unroll 4
-                for (int k = 0; k < kKBlocks * 4; ++k) {
-                    const uint64_t a = sdesc_sw128(sbase + kQOff + (k >> 2) * kQAtom + (k & 3) * 32,
-                                                   16, 1024);
-                    const uint64_t b = sdesc_sw128(kreg + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
-                    mma_pair_f16(tmem + 32 * st, a, b, id_s, k > 0 ? 1u : 0u);
+                            for (int k = 0; k < kKBlocks * 4; ++k) {
+                                const uint64_t a = sdesc_sw128(
+                                    sbase + kQOff + (k >> 2) * kQAtom + (k & 3) * 32, 16, 1024);
+                                const uint64_t b =
+                                    sdesc_sw128(kreg + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
+                                mma_pair_f16(tmem + 32 * sb, a, b, id_s, k > 0 ? 1u : 0u);
+                            }
+                            mma_commit_pair(mb + kBarSFull + 8 * sb, 0x3);
+                            mma_commit_pair(mb + kBarKEmpty + 8 * st, 0x3);
+                            ++sj;
+                            ++sg;
+                            did = true;
+                        }
+                    }
                 }
-                mma_commit_pair(mb + kBarSFull + 8 * st, 0x3);
-                mma_commit_pair(mb + kBarKEmpty + 8 * st, 0x3);
-                return true;
-            };
-            int gt = 0;
-            bool ok = true;
-            for (int ii = i_begin; ok && ii < i_end; ++ii) {
-                const ItemGeom g = item_geom(items, ii, seq_lens, bs, cap, flags, false);
-                const int ni = ii - i_begin;
-                if (!(ok = mbar_wait(mb + kBarQFull, ni & 1, flags, abort_flag))) break;
-                tc_fence_after();
-                if (g.n_tiles > 0) ok = issue_s(gt);
-                if (ok && g.n_tiles > 1) ok = issue_s(gt + 1);
-                for (int j = 0; ok && j < g.n_tiles; ++j) {
-                    const int gj = gt + j, st = gj & 1;
-                    if (!(ok = mbar_wait(mb + kBarPFull + 8 * st, (gj >> 1) & 1, flags, abort_flag)))
-                        break;
-                    if (j == 0 && ni >= 1 &&
-                        !(ok = mbar_wait(mb + kBarOFree, (ni - 1) & 1, flags, abort_flag)))
-                        break;
+                if (oj >= go.n_tiles) {
+                    mma_commit_pair(mb + kBarQFree, 0x3);  // every MMA of item oi issued
+                    if (++oi < n_items_w)
+                        go = item_geom(items, i_begin + oi, seq_lens, bs, cap, flags, false);
+                    oj = 0;
+                    did = true;
+                } else if (og < sg && mbar_try_wait(mb + kBarPFull + 8 * (og & 1), (og >> 1) & 1) &&
+                           (oj > 0 || oi == 0 || mbar_try_wait(mb + kBarOFree, (oi - 1) & 1))) {
                     tc_fence_after();
+                    const int st = og & 1;
                     const uint32_t vreg = sbase + kVOff + st * kVStage;
                     const uint32_t preg = sbase + kPOff + st * kPBytes;
 #pragma unroll
@@ -346,14 +373,31 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                                 vreg + (k >> 1) * 4 * kBox + (k & 1) * 2048 + i * 2 * kBox, kBox,
                                 1024);
                             mma_pair_f16(tmem + kTmemO + 128 * i, a, b, id_o,
-                                         (j > 0 || k > 0) ? 1u : 0u);
+                                         (oj > 0 || k > 0) ? 1u : 0u);
                         }
                     mma_commit_pair(mb + kBarODone + 8 * st, 0x3);
                     mma_commit_pair(mb + kBarVEmpty + 8 * st, 0x3);
-                    if (j + 2 < g.n_tiles) ok = issue_s(gj + 2);
+                    ++oj;
+                    ++og;
+                    did = true;
                 }
-                if (ok) mma_commit_pair(mb + kBarQFree, 0x3);
-                gt += g.n_tiles;
+                if (did) {
+                    idle_since = 0;
+                } else {
+                    const uint64_t now = globaltimer();
+                    if (idle_since == 0) {
+                        idle_since = now;
+                    } else if (*abort_flag ||
+                               (flags && (*reinterpret_cast<volatile int32_t*>(flags) &
+                                          PLKV_FLAG_TIMEOUT))) {
+                        *abort_flag = 1;
+                        break;
+                    } else if (now - idle_since > kWaitLimitNs) {
+                        set_flag(flags, PLKV_FLAG_TIMEOUT);
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
             }
         }
         __syncwarp();
@@ -375,13 +419,14 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
             for (int j = 0; j < g.n_tiles; ++j) {
                 const int gj = gt + j, st = gj & 1;
                 const int vc = min(kTile, g.t_end - (g.t_begin + kTile * j));
+                const int sb = gj % kSBufs;
                 if (ok)
-                    ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarSFull + 8 * st, (gj >> 1) & 1,
-                                                           flags, abort_flag));
+                    ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarSFull + 8 * sb,
+                                                           (gj / kSBufs) & 1, flags, abort_flag));
                 float s[32];
                 if (ok) {
                     tc_fence_after();
-                    tmem_ld32(tmem + lane_base + 32 * st, s);
+                    tmem_ld32(tmem + lane_base + 32 * sb, s);
                     tmem_wait_ld();
                 } else {
 #pragma unroll
