@@ -30,6 +30,7 @@ import importlib
 import json
 import math
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -63,6 +64,24 @@ def parse_args():
     ap.add_argument("--seqs", type=int, default=0,
                     help="keep only the first N sequences (small profiling cases)")
     return ap.parse_args()
+
+
+def profiled_traffic(mode: str, s, toks_local: int) -> int | None:
+    """DRAM bytes (read + write) of one partial-pass launch as captured by ncu
+    (profiles/latent_partial_<mode>_<workload>.md, line
+    `traffic_bytes_per_launch: N` for the full workload), scaled to the tokens
+    this rank's launch processes; None when no capture exists."""
+    path = os.path.join(ROOT, "profiles", f"latent_partial_{mode}_{s.name}.md")
+    try:
+        text = open(path, encoding="utf-8").read()
+    except OSError:
+        return None
+    m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", text, flags=re.M)
+    if not m:
+        return None
+    wl = importlib.import_module(PACKAGE + ".workloads")
+    full_tokens = int(np.sum(wl.initial_lens(s), dtype=np.int64))
+    return int(int(m.group(1)) * toks_local / max(full_tokens, 1))
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -408,8 +427,9 @@ def run_ours(args, s, rank: int, world: int):
                                // s.block_size)) * 4)
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
+    traffic = profiled_traffic(mode, s, toks_local)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                "frac": achieved / hbm_peak, "traffic": None, "kernel": f"latent partial ({mode})",
+                "frac": achieved / hbm_peak, "traffic": traffic, "kernel": f"latent partial ({mode})",
                 "kernel_ms": kern_ms, "bytes_per_launch": kern_bytes,
                 "peak_source": f"{peak_kind} hbm_gbs"}
     flops = wl.algorithmic_flops(s, lens_host, with_out_proj=False)

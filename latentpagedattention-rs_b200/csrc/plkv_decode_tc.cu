@@ -316,7 +316,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
             ItemGeom gs = n_items_w > 0 ? item_geom(items, i_begin, seq_lens, bs, cap, flags, false)
                                         : ItemGeom{0, 0, 0, 0};
             ItemGeom go = gs;
-            uint64_t idle_since = 0;
+            uint64_t idle_since = 0, next_check = 0;
             while (oi < n_items_w) {
                 bool did = false;
                 if (si < n_items_w) {
@@ -381,21 +381,30 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                     ++og;
                     did = true;
                 }
+                // Idle: the abort flag (shared memory) is checked on every
+                // pass, the global flag word and the time limit only every
+                // kFlagPollNs, so that polling stays a shared-memory loop.
                 if (did) {
                     idle_since = 0;
+                } else if (*abort_flag) {
+                    break;
                 } else {
                     const uint64_t now = globaltimer();
                     if (idle_since == 0) {
                         idle_since = now;
-                    } else if (*abort_flag ||
-                               (flags && (*reinterpret_cast<volatile int32_t*>(flags) &
-                                          PLKV_FLAG_TIMEOUT))) {
-                        *abort_flag = 1;
-                        break;
-                    } else if (now - idle_since > kWaitLimitNs) {
-                        set_flag(flags, PLKV_FLAG_TIMEOUT);
-                        *abort_flag = 1;
-                        break;
+                        next_check = now + kFlagPollNs;
+                    } else if (now >= next_check) {
+                        next_check = now + kFlagPollNs;
+                        if (flags && (*reinterpret_cast<volatile int32_t*>(flags) &
+                                      PLKV_FLAG_TIMEOUT)) {
+                            *abort_flag = 1;
+                            break;
+                        }
+                        if (now - idle_since > kWaitLimitNs) {
+                            set_flag(flags, PLKV_FLAG_TIMEOUT);
+                            *abort_flag = 1;
+                            break;
+                        }
                     }
                 }
             }

@@ -12,6 +12,7 @@ namespace plkv {
 namespace sm100 {
 
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait, then give up
+constexpr uint64_t kFlagPollNs = 20000ull;        // global flag word read every 20 us of waiting
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -63,9 +64,23 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 }
 
 // Arrive on a barrier given by its shared::cluster address (any CTA).
+//
+// The release is CTA-scoped.  A cluster-scoped release is a fence that waits
+// for every earlier memory operation of the thread to reach cluster-wide
+// visibility (about 1 us per arrive), and the data these arrives publish needs
+// none of it: it is this CTA's own shared memory (P tiles) or tensor memory
+// (the O accumulator that was read), complete once the writers passed a
+// fence.proxy.async / tcgen05.fence and a CTA barrier, and read afterwards
+// only by tensor-core operations that the peer issues after observing the
+// barrier phase.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+    asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];"
                  ::"r"(cluster_bar) : "memory");
+}
+
+// Plain arrive (no transaction bytes) on a barrier of this CTA.
+__device__ __forceinline__ void mbar_arrive_local(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -80,21 +95,43 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe of the same phase: unlike try_wait, test_wait never
+// suspends the thread, so a scheduler polling several barriers in turn does
+// not sleep on one while another is already complete.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs (or at once when another wait already gave up), records
-// PLKV_FLAG_TIMEOUT and returns false; the caller then abandons its work.
+// kWaitLimitNs (or soon after another wait, in this CTA or the peer, gave
+// up), records PLKV_FLAG_TIMEOUT and returns false; the caller then abandons
+// its work.  The global flag word is an L2 round trip, so it is read only
+// every kFlagPollNs of waiting: reading it between every two polls would
+// stretch each poll to that round trip and delay the waiter by as much.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* flags,
                                           volatile int* abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
+    uint64_t next_check = t0 + kFlagPollNs;
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
+        const uint64_t now = globaltimer();
+        if (now < next_check) continue;
+        next_check = now + kFlagPollNs;
         if (flags && (*reinterpret_cast<volatile int32_t*>(flags) & PLKV_FLAG_TIMEOUT)) {
             *abort_flag = 1;
             return false;
         }
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (now - t0 > kWaitLimitNs) {
             set_flag(flags, PLKV_FLAG_TIMEOUT);
             *abort_flag = 1;
             return false;

@@ -303,10 +303,10 @@ def test_model_shaped_workload(ops, pkg):
 
 # ---------------------------------------------- larger shapes vs FP64 oracle
 
-def _mla_case(pkg, batch, lens, seed=5):
+def _mla_case(pkg, batch, lens, seed=5, bs=64):
     """Absorbed-MLA shapes (Hq=128, L=576, Lv=512, D=128, bs=64), small batch."""
     rng = np.random.default_rng(seed)
-    bs, L, Lv, Hq, D = 64, 576, 512, 128, 128
+    L, Lv, Hq, D = 576, 512, 128, 128
     nb = [(n + bs - 1) // bs for n in lens]
     P = sum(nb) + 3
     perm = rng.permutation(P).astype(np.int32)
@@ -387,6 +387,35 @@ def test_tensor_core_matches_exact_mode(ops, pkg, workers):
     fin = torch.isfinite(le)
     assert torch.equal(fin, torch.isfinite(lt))
     assert rel_err(lt[fin], le[fin]) <= TC_REL
+
+
+@pytest.mark.parametrize("workers,bs", [(0, 64), (3, 64), (3, 32), (5, 128)])
+def test_tensor_core_ignores_nonfinite_slots_past_the_end(ops, pkg, workers, bs):
+    """Pool slots past a sequence's length (the rest of its last block, and
+    blocks no table names) hold NaN and Inf: the tensor-core pass reads whole
+    row groups there but must weigh them by exactly zero, as the exact pass,
+    which never reads them, does.  Block sizes 32 / 64 / 128 take the three
+    TMA box heights."""
+    lens = [777, 131, 4101, 64, 33, 320]
+    m = _mla_case(pkg, len(lens), lens, seed=17, bs=bs)
+    cache = m["cache"].reshape(-1, m["L"])          # [P * bs, L] view
+    used = np.zeros(cache.shape[0], bool)
+    for b, n in enumerate(lens):
+        for tok in range(n):
+            used[m["tables"][b, tok // m["bs"]] * m["bs"] + tok % m["bs"]] = True
+    bad = np.nonzero(~used)[0]
+    cache[bad[0::2]] = np.float16(np.nan)
+    cache[bad[1::2]] = np.float16(np.inf)
+    outs = {}
+    for mode in ("exact", "tc"):
+        plan = (ops.plan_workers(m["lens"], m["bs"], n_workers=workers) if mode == "tc" and workers
+                else ops.plan_splits(m["lens"], m["bs"]))
+        outs[mode] = ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]),
+                                       t(m["lens"]), plan, scale=m["scale"], value_dim=m["Lv"],
+                                       w_v=t(m["w_uv"]), mode=mode, want_lse=True)
+    assert torch.isfinite(outs["tc"]["ctx"]).all() and torch.isfinite(outs["tc"]["lse"]).all()
+    assert rel_err(outs["tc"]["ctx"].cpu(), outs["exact"]["ctx"].cpu()) <= TC_REL
+    assert rel_err(outs["tc"]["lse"].cpu(), outs["exact"]["lse"].cpu()) <= TC_REL
 
 
 def test_tensor_core_rejects_intermediates(ops, pkg):
