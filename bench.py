@@ -450,7 +450,12 @@ def run_ours(args, s, rank: int, world: int):
                              else "inputs smaller than L2",
                        "work_items": plan.n_items},
             "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
-            "clocks": clock_info}
+            "clocks": clock_info,
+            # persistent cache of the attended tokens: the latent pool against the
+            # FP16 K/V pool the same heads would need (memory_model.py)
+            "cache_bytes": importlib.import_module(PACKAGE + ".memory_model").cache_bytes_report(
+                tokens=int(global_lens.sum()), kv_heads=s.kv_heads, head_dim=D,
+                latent_dim=s.latent_dim)}
     if e2e:
         line["e2e"] = {"value": algo / (e2e["ms_per_step"] * 1e-3) / 1e12, "unit": "TB/s",
                        "ms_per_step": e2e["ms_per_step"],

@@ -7,10 +7,11 @@ root on ``sys.path``).  All computation runs in ``libplkv_b200.so`` (C ABI in
 ``include/plkv_b200.h``); importing the operations fails if it is not built.
 """
 
-from . import block_table, workloads  # noqa: F401  (pure host modules)
+from . import block_table, memory_model, workloads  # noqa: F401  (pure host modules)
 from .block_table import PagedBlockTable, logical_blocks_for_seq_len  # noqa: F401
 
-__all__ = ["PagedBlockTable", "logical_blocks_for_seq_len", "block_table", "workloads", "ops"]
+__all__ = ["PagedBlockTable", "logical_blocks_for_seq_len", "block_table", "memory_model",
+           "workloads", "ops"]
 
 
 def __getattr__(name):
