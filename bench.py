@@ -3,13 +3,19 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
                     [--mode exact|tc] [--impl ours|reference] [--with-wo]
+                    [--no-graph] [--grow]
 
 A step is one append + decode pass over the whole batch: one FP32 latent row
 per sequence is written into the FP16 cache through its block table (the
 same slot every step, so the attended length stays fixed), then the split-K
 decode (scores, mask, online softmax, latent context) and the log-sum-exp
 combine with the W_uv / W_v projection run; `--with-wo` adds the W_o output
-projection.  The default workload is the long-context one (8 sequences of
+projection.  `--grow` makes every step append a new token per sequence
+instead: its position is allocated on the device (block table, length and
+pool counter advance there), as in the reference's write-then-attend loop.
+On one GPU the step is recorded once into a CUDA graph and replayed
+(`--no-graph` launches it eagerly); the partial pass's kernel time always
+comes from CUDA events around it in the eager steps that precede the replays.  The default workload is the long-context one (8 sequences of
 131072 tokens, absorbed-MLA shapes: 128 heads, latent 512 + 64, block 64).
 
 Metric: achieved HBM TB/s = algorithmic bytes of the step / step time (the
@@ -61,6 +67,12 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU work of the bounded CPU-baseline sample")
+    ap.add_argument("--graph", dest="graph", action="store_true", default=None,
+                    help="replay the step from a CUDA graph (default on one GPU; the kernel "
+                         "time comes from the eager steps)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false")
+    ap.add_argument("--grow", action="store_true",
+                    help="append a new token per sequence each step (device allocator)")
     ap.add_argument("--seqs", type=int, default=0,
                     help="keep only the first N sequences (small profiling cases)")
     return ap.parse_args()
@@ -261,14 +273,25 @@ def run_ours(args, s, rank: int, world: int):
     ops = importlib.import_module(PACKAGE + ".ops")
     wl = importlib.import_module(PACKAGE + ".workloads")
     mg = importlib.import_module(PACKAGE + ".multigpu")
+    dl = importlib.import_module(PACKAGE + ".decode_loop")
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     mode = args.mode
     if mode == "auto":
         mode = "tc" if (s.absorbed and ops.tc_available(s)) else "exact"
     split_k = world > 1 and s.name in SPLIT_K_WORKLOADS
+    if args.graph is None:
+        # default: graphs wherever the step holds no collective
+        args.graph = not split_k
+    if split_k and (args.graph or args.grow):
+        raise SystemExit("--graph / --grow: not with the split-K shards of this workload")
+    D = s.head_dim
+    # --grow: every step allocates one new token per sequence on the device;
+    # room for all the steps this run takes (warm-up, eager, graph, e2e).
+    grow_steps = args.warmup + 3 * args.steps + 16 if args.grow else 0
+    extra_blocks = s.batch * (grow_steps // s.block_size + 2) if args.grow else 0
     x = wl.device_inputs(s, dev, shards=world if split_k else 1, shard=rank if split_k else 0,
-                         with_out_proj=args.with_wo)
+                         with_out_proj=args.with_wo, extra_blocks=extra_blocks)
     global_lens = x["global_lens"]
     B = s.batch
     seqs = np.arange(B)
@@ -290,63 +313,104 @@ def run_ours(args, s, rank: int, world: int):
         positions = None
     else:
         positions = torch.as_tensor(gpos.astype(np.int32), device=dev)
-    plan = (ops.plan_workers(lens_host, s.block_size, device=dev) if mode == "tc"
-            else ops.plan_splits(lens_host, s.block_size, device=dev))
-    D = s.head_dim
-    ctx = torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
-    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, nb_local, s.q_heads, s.latent_dim,
-                                                s.value_dim),
-                     dtype=torch.uint8, device=dev)
-    want_lse = split_k
-    gathered_ctx = torch.empty((world, nb_local, s.q_heads, D), dtype=torch.float32,
-                               device=dev) if split_k else None
-    gathered_lse = torch.empty((world, nb_local, s.q_heads), dtype=torch.float32,
-                               device=dev) if split_k else None
     w_o = x.get("w_o")
-    out = (torch.empty((nb_local, s.out_dim), dtype=torch.float32, device=dev)
-           if w_o is not None else None)
-    wo_ws = None
+    if args.grow:
+        lens0 = lens_host.astype(np.int64) - 1     # tokens stored before the first step
+        cap = lens0 + grow_steps
+        width = int((cap.max() + s.block_size - 1) // s.block_size)
+        keep = (lens0 + s.block_size - 1) // s.block_size
+        tab = tables.cpu().numpy()
+        t_host = np.full((nb_local, width), -1, np.int32)
+        for i in range(nb_local):
+            t_host[i, :keep[i]] = tab[i, :keep[i]]
+        g_lens = torch.as_tensor(lens0.astype(np.int32), device=dev)
+        # new blocks come from the free ids that follow the pre-filled pool
+        g_next = torch.tensor([x["pool"]], dtype=torch.int32, device=dev)
+        loop = dl.PagedLatentDecodeLoop(
+            x["cache"], torch.as_tensor(t_host, device=dev), g_lens, g_next, q_heads=s.q_heads,
+            scale=s.scale, max_new_tokens=grow_steps, w_v=x["w_v"], value_dim=s.value_dim,
+            w_k=None if s.absorbed else x["w_k"], w_o=w_o, mode=mode, seq_lens_host=lens0)
+        loop.q[0].copy_(q_in)
+        loop.rows[0].copy_(new_rows)
+        q_buf, rows_buf = loop.q[0], loop.rows[0]
+        plan = loop.plan
+        launches_per_step = loop.launches_per_step
 
-    def step(q_src, rows_src, ev=None):
-        nonlocal wo_ws
-        if split_k:
-            ops.latent_append_slots(rows_src, x["cache"], slots_d)
-        else:
-            ops.latent_append(rows_src, x["cache"], tables, positions=positions)
-        q_lat = q_src if s.absorbed else ops.project_query(q_src, x["w_k"])
-        if ev is not None:
-            ev[0].record()
-        r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
-                              value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
-                              want_lse=want_lse, workspace=ws, allow_empty=split_k,
-                              phase="partial")
-        if ev is not None:
-            ev[1].record()
-        r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
-                              value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
-                              want_lse=want_lse, workspace=ws, allow_empty=split_k,
-                              phase="combine")
-        res = ctx
-        if split_k:
-            res = mg.gather_and_merge(ctx, r["lse"], world, lambda c, l: ops.lse_merge(c, l)[0],
-                                      gathered_ctx, gathered_lse)
+        def run_step(ev=None):
+            if ev is not None:
+                loop.partial_events = [ev]
+            return loop.step()[0]
+    else:
+        plan = (ops.plan_workers(lens_host, s.block_size, device=dev) if mode == "tc"
+                else ops.plan_splits(lens_host, s.block_size, device=dev))
+        ctx = torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
+        ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, nb_local, s.q_heads,
+                                                    s.latent_dim, s.value_dim),
+                         dtype=torch.uint8, device=dev)
+        want_lse = split_k
+        gathered_ctx = torch.empty((world, nb_local, s.q_heads, D), dtype=torch.float32,
+                                   device=dev) if split_k else None
+        gathered_lse = torch.empty((world, nb_local, s.q_heads), dtype=torch.float32,
+                                   device=dev) if split_k else None
+        out = (torch.empty((nb_local, s.out_dim), dtype=torch.float32, device=dev)
+               if w_o is not None else None)
+        q_lat_buf = (None if s.absorbed else
+                     torch.empty((nb_local, s.q_heads, s.latent_dim), dtype=torch.float32,
+                                 device=dev))
+        wo_splits = wo_ws = None
         if w_o is not None:
-            if wo_ws is None:
-                wo_ws = torch.empty(1, dtype=torch.uint8, device=dev)
-            o = ops.out_proj(res.reshape(nb_local, -1), w_o, out=out)
-            res = o
-        return res
+            wo_splits = ops.default_out_proj_splits(w_o.shape[0], w_o.shape[1], dev)
+            wo_ws = torch.empty(max(1, ops.out_proj_workspace_bytes(nb_local, w_o.shape[1],
+                                                                    wo_splits)),
+                                dtype=torch.uint8, device=dev)
 
-    launches_per_step = 3 + (0 if s.absorbed else 1) + (1 if split_k else 0) + \
-        (2 if w_o is not None else 0)
+        def step(q_src, rows_src, ev=None):
+            if split_k:
+                ops.latent_append_slots(rows_src, x["cache"], slots_d)
+            else:
+                ops.latent_append(rows_src, x["cache"], tables, positions=positions)
+            q_lat = q_src if s.absorbed else ops.project_query(q_src, x["w_k"], out=q_lat_buf)
+            if ev is not None:
+                ev[0].record()
+            r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
+                                  value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
+                                  want_lse=want_lse, workspace=ws, allow_empty=split_k,
+                                  phase="partial")
+            if ev is not None:
+                ev[1].record()
+            r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
+                                  value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
+                                  want_lse=want_lse, workspace=ws, allow_empty=split_k,
+                                  phase="combine")
+            res = ctx
+            if split_k:
+                res = mg.gather_and_merge(ctx, r["lse"], world,
+                                          lambda c, l: ops.lse_merge(c, l)[0],
+                                          gathered_ctx, gathered_lse)
+            if w_o is not None:
+                res = ops.out_proj(res.reshape(nb_local, -1), w_o, out=out, k_splits=wo_splits,
+                                   workspace=wo_ws)
+            return res
+
+        q_buf, rows_buf = q_in, new_rows
+
+        def run_step(ev=None):
+            return step(q_buf, rows_buf, ev)
+
+        # append, partial pass (+ FP16 query staging in tensor-core mode),
+        # combine, query projection, shard merge, W_o GEMM + split reduction
+        launches_per_step = (3 + (mode == "tc") + (0 if s.absorbed else 1) + (1 if split_k else 0)
+                             + (2 if w_o is not None else 0))
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[dev.index])
         torch.cuda.synchronize(dev)
 
+    steps_done = 0
     for _ in range(args.warmup):
-        step(q_in, new_rows)
+        run_step()
+    steps_done += args.warmup
     barrier()
     uuid = None
     try:
@@ -358,47 +422,86 @@ def run_ours(args, s, rank: int, world: int):
         clocks.start()
         time.sleep(0.3)
     barrier()
+    # Eager steps, with CUDA events around the partial pass of each one.
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
+    timed_from = steps_done
     start.record()
     for i in range(args.steps):
-        step(q_in, new_rows, kev[i])
+        run_step(kev[i])
     end.record()
     barrier()
-    elapsed_ms = start.elapsed_time(end)
+    steps_done += args.steps
+    eager_ms = start.elapsed_time(end)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    elapsed_ms = eager_ms
+    stepper = run_step
+    if args.graph:
+        # The same step recorded once into a CUDA graph and replayed.
+        if args.grow:
+            loop.capture()
+
+            def stepper():
+                return loop.step()[0]
+        else:
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                g_res = step(q_buf, rows_buf)
+
+            def stepper():
+                graph.replay()
+                return g_res
+        for _ in range(3):
+            stepper()
+        steps_done += 3
+        barrier()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        timed_from = steps_done
+        g0.record()
+        for _ in range(args.steps):
+            stepper()
+        g1.record()
+        barrier()
+        steps_done += args.steps
+        elapsed_ms = g0.elapsed_time(g1)
     clock_info = clocks.stop() if clocks else None
-    t = torch.tensor([elapsed_ms, kern_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([elapsed_ms, kern_ms, eager_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, kern_ms = float(t[0]), float(t[1])
+    elapsed_ms, kern_ms, eager_ms = float(t[0]), float(t[1]), float(t[2])
     ms_per_step = elapsed_ms / args.steps
+    # Lengths attended in the middle of the timed steps (they grow by one a
+    # step with --grow).
+    attended = (lens_host.astype(np.int64) + (timed_from + args.steps // 2 if args.grow else 0))
+    attended_global = (global_lens.astype(np.int64)
+                       + (timed_from + args.steps // 2 if args.grow else 0))
 
     # End to end through the public API with host buffers: H2D of the step's
     # query and new rows, the step, D2H of the result.
     e2e = None
     if not args.no_e2e:
-        q_host = q_in.cpu().pin_memory()
-        rows_host = new_rows.cpu().pin_memory()
-        q_dev = torch.empty_like(q_in)
-        rows_dev = torch.empty_like(new_rows)
-        res_shape = (nb_local, s.out_dim) if w_o is not None else (nb_local, s.q_heads, D)
-        res_host = torch.empty(res_shape, dtype=torch.float32).pin_memory()
+        q_host = q_buf.cpu().pin_memory()
+        rows_host = rows_buf.cpu().pin_memory()
+        res0 = stepper()
+        steps_done += 1
+        res_host = torch.empty(tuple(res0.shape), dtype=torch.float32).pin_memory()
         for _ in range(2):
-            q_dev.copy_(q_host, non_blocking=True)
-            rows_dev.copy_(rows_host, non_blocking=True)
-            res_host.copy_(step(q_dev, rows_dev), non_blocking=True)
+            q_buf.copy_(q_host, non_blocking=True)
+            rows_buf.copy_(rows_host, non_blocking=True)
+            res_host.copy_(stepper(), non_blocking=True)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         n_e2e = max(3, args.steps // 2)
         e0.record()
         for _ in range(n_e2e):
-            q_dev.copy_(q_host, non_blocking=True)
-            rows_dev.copy_(rows_host, non_blocking=True)
-            res_host.copy_(step(q_dev, rows_dev), non_blocking=True)
+            q_buf.copy_(q_host, non_blocking=True)
+            rows_buf.copy_(rows_host, non_blocking=True)
+            res_host.copy_(stepper(), non_blocking=True)
         e1.record()
         barrier()
         te = torch.tensor([e0.elapsed_time(e1) / n_e2e], dtype=torch.float64, device=dev)
@@ -417,14 +520,13 @@ def run_ours(args, s, rank: int, world: int):
     if rank != 0:
         return None
     peaks, peak_kind = load_peaks()
-    algo = wl.algorithmic_bytes(s, global_lens, with_out_proj=w_o is not None)
+    algo = wl.algorithmic_bytes(s, attended_global, with_out_proj=w_o is not None)
     value = algo / (ms_per_step * 1e-3) / 1e12
     # Roofline of the dominant kernel (split-K partial pass on rank 0):
     # latent rows attended x L x 2 bytes + query + table entries, per launch.
-    toks_local = int(np.sum(lens_host, dtype=np.int64))
+    toks_local = int(np.sum(attended, dtype=np.int64))
     kern_bytes = (toks_local * s.latent_dim * 2 + nb_local * s.q_heads * s.latent_dim * 4
-                  + int(np.sum((lens_host.astype(np.int64) + s.block_size - 1)
-                               // s.block_size)) * 4)
+                  + int(np.sum((attended + s.block_size - 1) // s.block_size)) * 4)
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
     traffic = profiled_traffic(mode, s, toks_local)
@@ -432,7 +534,7 @@ def run_ours(args, s, rank: int, world: int):
                 "frac": achieved / hbm_peak, "traffic": traffic, "kernel": f"latent partial ({mode})",
                 "kernel_ms": kern_ms, "bytes_per_launch": kern_bytes,
                 "peak_source": f"{peak_kind} hbm_gbs"}
-    flops = wl.algorithmic_flops(s, lens_host, with_out_proj=False)
+    flops = wl.algorithmic_flops(s, attended, with_out_proj=False)
     roofline["achieved_tflops"] = flops / (kern_ms * 1e-3) / 1e12
     line = {"metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -443,7 +545,11 @@ def run_ours(args, s, rank: int, world: int):
             "config": {"workload": s.name, "mode": mode, "batch": s.batch,
                        "q_heads": s.q_heads, "latent_dim": s.latent_dim,
                        "value_dim": s.value_dim, "head_dim": D, "block_size": s.block_size,
-                       "tokens": int(global_lens.sum()), "w_o": w_o is not None,
+                       "tokens": int(attended_global.sum()), "w_o": w_o is not None,
+                       "cuda_graph": bool(args.graph),
+                       "ms_per_step_eager": eager_ms / args.steps,
+                       "growing": ("one token per sequence allocated on the device each step"
+                                   if args.grow else "no: the append rewrites the last token"),
                        "parallelism": (f"split-k{world}" if split_k else
                                        (f"dp{world}" if world > 1 else "single")),
                        "l2": "inputs larger than L2 (no flush)" if algo > 126e6

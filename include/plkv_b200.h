@@ -98,6 +98,26 @@ int plkv_latent_append_slots_f16(const float* rows, const int64_t* slots, int64_
                                  uint16_t* cache, int64_t num_slots, int32_t latent_dim,
                                  int32_t* err_flags, plkv_stream_t stream);
 
+/* Device-side allocation of new token positions (replaces the bump allocator
+ * PagedBlockTable.allocate_token_positions, block_table.py:26-38, and
+ * BlockTable::allocate_tokens, lib.rs:1346-1364, for a batch on the GPU).
+ * Sequence b gets counts[b] new tokens (counts NULL: one each) at positions
+ * seq_lens[b], seq_lens[b]+1, ...; a logical block whose table entry is < 0
+ * takes the next physical block of the shared counter *next_block (blocks
+ * are handed out in sequence order, then logical order).  Writes the slot
+ * (physical * block_size + offset) of every new token to slots[sum(counts)]
+ * in sequence order, stores the new blocks in block_tables, advances
+ * seq_lens and *next_block.  Blocks past num_physical or past max_blocks are
+ * not handed out: their tokens get slot -1 (the slot append skips them) and
+ * PLKV_FLAG_BAD_BLOCK / PLKV_FLAG_BAD_POSITION is raised.  Slots past
+ * max_slots (the capacity of slots) are not written (PLKV_FLAG_BAD_POSITION).
+ * One CTA; stream ordered, no host synchronisation (capturable in a CUDA
+ * graph). */
+int plkv_allocate_slots(int32_t* block_tables, int64_t max_blocks, int32_t* seq_lens,
+                        const int32_t* counts, int32_t batch, int32_t block_size,
+                        int32_t* next_block, int64_t num_physical, int64_t* slots,
+                        int64_t max_slots, int32_t* err_flags, plkv_stream_t stream);
+
 /* Writes one K row and one V row ([kv_heads, head_dim] FP32 each) per request
  * into FP16 head-major caches [num_physical, kv_heads, block_size, head_dim]
  * (the layout of lib.rs:1232).  Replaces paged_kv_write_f32 (lib.rs:190-247)

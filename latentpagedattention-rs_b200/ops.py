@@ -168,6 +168,39 @@ def latent_append_slots(rows: torch.Tensor, cache: torch.Tensor, slots: torch.Te
           "plkv_latent_append_slots_f16")
 
 
+def allocate_slots(block_tables: torch.Tensor, seq_lens: torch.Tensor, next_block: torch.Tensor,
+                   num_physical: int, block_size: int, *, counts: torch.Tensor | None = None,
+                   n_new: int | None = None, slots: torch.Tensor | None = None,
+                   flags: torch.Tensor | None = None) -> torch.Tensor:
+    """Device-side bump allocation of new token positions for a batch
+    (PagedBlockTable.allocate_token_positions, block_table.py:26-38, on the
+    GPU): advances `seq_lens` in place, stores new blocks in `block_tables`
+    (entries < 0 are "no block yet") and the pool counter `next_block` ([1]
+    int32), and returns the slot of every new token (int64, sequence order).
+    `counts` ([B] int32, default one token per sequence) needs `n_new` (their
+    sum) so that nothing synchronises with the host."""
+    _need_cuda("block_tables", block_tables, torch.int32)
+    _need_cuda("seq_lens", seq_lens, torch.int32)
+    _need_cuda("next_block", next_block, torch.int32)
+    B = seq_lens.shape[0]
+    if counts is not None:
+        _need_cuda("counts", counts, torch.int32)
+        if n_new is None:
+            raise ValueError("n_new (the sum of counts) is required with counts")
+    total = B if counts is None else int(n_new)
+    if slots is None:
+        slots = torch.empty(max(total, 1), dtype=torch.int64, device=seq_lens.device)
+    _need_cuda("slots", slots, torch.int64)
+    if slots.numel() < total:
+        raise ValueError(f"slots holds {slots.numel()} entries, {total} tokens are allocated")
+    check(lib().plkv_allocate_slots(_ptr(block_tables), block_tables.shape[1], _ptr(seq_lens),
+                                    _ptr(counts), B, block_size, _ptr(next_block), num_physical,
+                                    _ptr(slots), slots.numel(), _ptr(flags),
+                                    _stream(seq_lens.device)),
+          "plkv_allocate_slots")
+    return slots[:total]
+
+
 def kv_append(k_rows: torch.Tensor, v_rows: torch.Tensor, k_cache: torch.Tensor,
               v_cache: torch.Tensor, block_tables: torch.Tensor, *,
               positions: torch.Tensor | None = None, seq_lens: torch.Tensor | None = None,
@@ -300,7 +333,8 @@ def plan_workers(seq_lens_host, block_size: int, *, n_workers: int | None = None
 
 # ------------------------------------------------------------------- decode
 
-def project_query(q: torch.Tensor, w_k_head_major: torch.Tensor) -> torch.Tensor:
+def project_query(q: torch.Tensor, w_k_head_major: torch.Tensor, *,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
     """q_lat[b, h] = W_k[kv(h)] q[b, h] (lib.rs:1026-1032), W_k [KV, L, D]."""
     _need_cuda("q", q, torch.float32)
     _need_cuda("w_k", w_k_head_major, torch.float32)
@@ -308,7 +342,12 @@ def project_query(q: torch.Tensor, w_k_head_major: torch.Tensor) -> torch.Tensor
     KV, L, D2 = w_k_head_major.shape
     if D2 != D:
         raise ValueError("head_dim mismatch between q and W_k")
-    q_lat = torch.empty((B, Hq, L), dtype=torch.float32, device=q.device)
+    if out is None:
+        out = torch.empty((B, Hq, L), dtype=torch.float32, device=q.device)
+    _need_cuda("out", out, torch.float32)
+    if tuple(out.shape) != (B, Hq, L):
+        raise ValueError(f"out must have shape {(B, Hq, L)}")
+    q_lat = out
     check(lib().plkv_project_query(_ptr(q), _ptr(w_k_head_major), _ptr(q_lat), B, Hq, KV, D, L,
                                    _stream(q.device)), "plkv_project_query")
     return q_lat
@@ -442,6 +481,18 @@ def lse_merge(ctx_shards: torch.Tensor, lse_shards: torch.Tensor,
     return out, lse_out
 
 
+def default_out_proj_splits(in_dim: int, out_dim: int, device: torch.device | None = None) -> int:
+    """Split of the contracted dimension of the W_o GEMM: about four CTAs per
+    SM over the 128-column tiles, at least 64 rows of W_o per split."""
+    tiles = (out_dim + 127) // 128
+    k_splits = max(1, min(64, (2 * default_target_items(device)) // max(tiles, 1)))
+    return min(k_splits, max(1, in_dim // 64))
+
+
+def out_proj_workspace_bytes(batch: int, out_dim: int, k_splits: int) -> int:
+    return int(lib().plkv_out_proj_workspace_size(batch, out_dim, k_splits))
+
+
 def out_proj(x: torch.Tensor, w_o: torch.Tensor, *, out: torch.Tensor | None = None,
              k_splits: int | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """W_o output projection ``out = x @ w_o`` in FP32 (x [B, in], w_o [in, out])."""
@@ -452,9 +503,7 @@ def out_proj(x: torch.Tensor, w_o: torch.Tensor, *, out: torch.Tensor | None = N
     if K2 != K:
         raise ValueError("W_o rows must equal the concatenated head width")
     if k_splits is None:
-        tiles = (N + 127) // 128
-        k_splits = max(1, min(64, (2 * default_target_items(x.device)) // max(tiles, 1)))
-        k_splits = min(k_splits, max(1, K // 64))
+        k_splits = default_out_proj_splits(K, N, x.device)
     if out is None:
         out = torch.empty((B, N), dtype=torch.float32, device=x.device)
     need = int(lib().plkv_out_proj_workspace_size(B, N, k_splits))

@@ -152,12 +152,15 @@ def head_major(w_canonical: np.ndarray, heads: int, head_dim: int) -> np.ndarray
 
 
 def device_inputs(s: WorkloadSpec, device, *, shards: int = 1, shard: int = 0,
-                  with_out_proj: bool = True, with_fullkv: bool = False) -> dict:
+                  with_out_proj: bool = True, with_fullkv: bool = False,
+                  extra_blocks: int = 0) -> dict:
     """Inputs of any workload generated on a CUDA device (torch generator).
 
     With ``shards > 1`` the cache holds only shard ``shard``'s blocks of every
     sequence; ``lens`` are then the shard-local lengths and ``global_lens``
     the full ones.  The query and the weights are identical on every shard.
+    ``extra_blocks`` free blocks follow the ``pool`` blocks the tables draw
+    from (ids pool .. pool + extra_blocks - 1), for a loop that allocates.
     """
     import torch
 
@@ -167,10 +170,11 @@ def device_inputs(s: WorkloadSpec, device, *, shards: int = 1, shard: int = 0,
     L, Lv, D, Hq = s.latent_dim, s.value_dim, s.head_dim, s.q_heads
     g = torch.Generator(device=dev)
     g.manual_seed(s.seed * 1000 + 17 * shard + 3)
-    cache = torch.empty((pool, s.block_size, L), dtype=torch.float16, device=dev)
+    total = pool + int(extra_blocks)
+    cache = torch.empty((total, s.block_size, L), dtype=torch.float16, device=dev)
     chunk = max(1, (1 << 26) // (s.block_size * L))
-    for i in range(0, pool, chunk):
-        j = min(pool, i + chunk)
+    for i in range(0, total, chunk):
+        j = min(total, i + chunk)
         cache[i:j] = (torch.randn((j - i, s.block_size, L), generator=g, device=dev)
                       * s.cache_std).half()
     gw = torch.Generator(device=dev)

@@ -408,3 +408,40 @@ def fullkv_decode_batch_f64(q, k_f16, v_f16, tables, lens, block_size, scale, gr
         probs.append(p)
         ctx[b] = np.einsum("ht,htd->hd", p, vh)
     return scores, probs, ctx
+
+
+# ------------------------------------------------------------ block_table.py
+
+def allocate_token_positions_batch(tables: np.ndarray, lens: np.ndarray, counts: np.ndarray,
+                                   next_block: int, block_size: int, num_physical: int):
+    """Batched form of PagedBlockTable.allocate_token_positions
+    (block_table.py:26-38): sequences in batch order, each taking ``counts[b]``
+    new positions; a logical block without a physical block (entry < 0) takes
+    the pool's next block id (one counter shared by the batch, where the
+    reference keeps one per table).  Ids at or past ``num_physical`` are not
+    stored (pool exhausted) and positions that land in no valid block get slot
+    -1.  Returns (tables, lens, slots, next_block); slot = physical * bs + offset.
+    """
+    tables = np.array(tables, dtype=np.int32, copy=True)
+    lens = np.array(lens, dtype=np.int32, copy=True)
+    max_blocks = tables.shape[1]
+    slots = []
+    nb = int(next_block)
+    for b in range(lens.size):
+        c = int(counts[b])
+        if c <= 0:
+            continue
+        first, last = int(lens[b]) // block_size, (int(lens[b]) + c - 1) // block_size
+        for lb in range(first, last + 1):
+            if lb < max_blocks and tables[b, lb] < 0:
+                if nb < num_physical:
+                    tables[b, lb] = nb
+                nb += 1
+        for i in range(c):
+            pos = int(lens[b]) + i
+            lb = pos // block_size
+            phys = int(tables[b, lb]) if lb < max_blocks else -1
+            ok = 0 <= phys < num_physical
+            slots.append(phys * block_size + pos % block_size if ok else -1)
+        lens[b] += c
+    return tables, lens, np.asarray(slots, dtype=np.int64), nb

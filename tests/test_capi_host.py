@@ -121,6 +121,14 @@ def test_host_validation_before_launch():
     assert L.plkv_out_proj(fake, fake, fake, 65, 16, 16, 1, fake, 1 << 20, None) == \
         m.PLKV_ERR_UNSUPPORTED
     assert L.plkv_latent_decode_workspace_size(10, 2, 4, 8, 8) > 10 * 4 * 8 * 4
+    assert L.plkv_allocate_slots(fake, 4, fake, None, 0, 16, fake, 64, fake, 4, None, None) == \
+        m.PLKV_ERR_ZERO_VALUE
+    assert L.plkv_allocate_slots(None, 4, fake, None, 2, 16, fake, 64, fake, 4, None, None) == \
+        m.PLKV_ERR_INVALID_ARGUMENT
+    assert L.plkv_allocate_slots(fake, 4, fake, None, 2, 16, fake, 1 << 40, fake, 4, None, None) == \
+        m.PLKV_ERR_ARITHMETIC_OVERFLOW
+    assert L.plkv_allocate_slots(fake, 4, fake, None, 2, 16, fake, 64, fake, 0, None, None) == \
+        m.PLKV_ERR_ZERO_VALUE
 
 
 def test_product_never_imports_the_oracle():

@@ -102,3 +102,47 @@ def test_algorithmic_bytes_long_context(pkg):
     assert latent == 1_207_959_552
     assert b - latent == (128 * 512 * 128 * 4 + 8 * 128 * 576 * 4 + 8 * 128 * 128 * 4
                           + 8 * 576 * 6 + 8 * 2048 * 4)
+
+
+def test_batched_allocation_oracle_matches_block_table(pkg):
+    """oracle.np_ref.allocate_token_positions_batch against the reference's
+    fixtures and, sequence by sequence, PagedBlockTable with the counter the
+    earlier sequences left (block_table.py:26-38)."""
+    from oracle.np_ref import allocate_token_positions_batch as alloc
+
+    for name in ("block_table_seq5_block2.json", "block_table_seq128_block16.json"):
+        fx = load_reference_fixture(name)
+        bs, n = fx["block_size"], fx["seq_len"]
+        tables, lens, slots, nb = alloc(np.full((1, 64), -1, np.int32), np.zeros(1, np.int32),
+                                        np.array([n], np.int32), 0, bs, 1 << 20)
+        assert list(tables[0, :len(fx["logical_blocks"])]) == fx["logical_blocks"]
+        for loc in fx["token_locations"]:
+            assert slots[loc["token"]] == loc["physical_block"] * bs + loc["offset"]
+        assert lens[0] == n and nb == len(fx["logical_blocks"])
+
+    rng = np.random.default_rng(3)
+    bs, B = 8, 9
+    tables = np.full((B, 12), -1, np.int32)
+    lens = np.zeros(B, np.int32)
+    refs = [None] * B
+    nb = 0
+    for _ in range(4):                                   # four rounds of uneven appends
+        counts = rng.integers(0, 20, B).astype(np.int32)
+        tables, lens, slots, nb2 = alloc(tables, lens, counts, nb, bs, 1 << 20)
+        k = 0
+        for b in range(B):
+            if counts[b] == 0:
+                continue
+            if refs[b] is None:
+                refs[b] = pkg.PagedBlockTable(bs, first_physical_block=nb)
+            refs[b].next_physical_block = nb             # the shared counter
+            got = refs[b].allocate_token_positions(int(counts[b]))
+            nb = refs[b].next_physical_block
+            assert list(slots[k:k + counts[b]]) == [p * bs + o for _, p, o in got]
+            k += counts[b]
+            assert list(tables[b, :refs[b].num_blocks]) == refs[b].to_list()
+        assert nb == nb2 and k == slots.size
+    # pool exhaustion: ids at or past num_physical are not stored, slots are -1
+    t2, _, s2, nb3 = alloc(np.full((1, 4), -1, np.int32), np.zeros(1, np.int32),
+                           np.array([10], np.int32), 0, 4, 2)
+    assert list(t2[0]) == [0, 1, -1, -1] and list(s2[8:]) == [-1, -1] and nb3 == 3
