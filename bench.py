@@ -73,6 +73,9 @@ def parse_args():
     ap.add_argument("--no-graph", dest="graph", action="store_false")
     ap.add_argument("--grow", action="store_true",
                     help="append a new token per sequence each step (device allocator)")
+    ap.add_argument("--path", default="latent", choices=["latent", "fullkv", "materialised"],
+                    help="latent: the direct latent decode; fullkv: stored FP16 K/V; "
+                         "materialised: K/V rebuilt from the latent pool every step")
     ap.add_argument("--seqs", type=int, default=0,
                     help="keep only the first N sequences (small profiling cases)")
     return ap.parse_args()
@@ -285,6 +288,8 @@ def run_ours(args, s, rank: int, world: int):
         args.graph = not split_k
     if split_k and (args.graph or args.grow):
         raise SystemExit("--graph / --grow: not with the split-K shards of this workload")
+    if args.path != "latent" and (s.absorbed or split_k or args.grow):
+        raise SystemExit("--path fullkv / materialised: one-GPU GQA workloads with W_k, no --grow")
     D = s.head_dim
     # --grow: every step allocates one new token per sequence on the device;
     # room for all the steps this run takes (warm-up, eager, graph, e2e).
@@ -340,6 +345,75 @@ def run_ours(args, s, rank: int, world: int):
             if ev is not None:
                 loop.partial_events = [ev]
             return loop.step()[0]
+    elif args.path != "latent":
+        # Comparison points on the same shapes: stored FP16 K/V ("fullkv": the
+        # step appends K/V rows and decodes them) and K/V rebuilt from the
+        # latent pool every step ("materialised": latent append, then K/V of
+        # every active token, then the same full-KV decode).
+        KV, bs = s.kv_heads, s.block_size
+        P = x["cache"].shape[0]
+        plan = ops.plan_splits(lens_host, bs, device=dev)
+        ctx = torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
+        fws = torch.empty(int(ops.lib().plkv_fullkv_decode_workspace_size(
+            plan.n_items, nb_local, s.q_heads, D)), dtype=torch.uint8, device=dev)
+        if args.path == "fullkv":
+            kv = wl.fullkv_from_latent(s, x, dev)
+            k_cache, v_cache = kv["k_cache"], kv["v_cache"]
+            gk = torch.Generator(device=dev)
+            gk.manual_seed(s.seed * 1000 + 5)
+            k_rows = torch.randn((nb_local, KV, D), generator=gk, device=dev)
+            v_rows = torch.randn((nb_local, KV, D), generator=gk, device=dev)
+        else:
+            k_cache = torch.zeros((P, KV, bs, D), dtype=torch.float16, device=dev)
+            v_cache = torch.zeros_like(k_cache)
+            tab = tables.cpu().numpy()
+            act = np.concatenate([tab[i, np.arange(n) // bs].astype(np.int64) * bs
+                                  + np.arange(n) % bs for i, n in enumerate(lens_host)])
+            act_slots = torch.as_tensor(act, device=dev)
+        out = (torch.empty((nb_local, s.out_dim), dtype=torch.float32, device=dev)
+               if w_o is not None else None)
+        wo_splits = wo_ws = None
+        if w_o is not None:
+            wo_splits = ops.default_out_proj_splits(w_o.shape[0], w_o.shape[1], dev)
+            wo_ws = torch.empty(max(1, ops.out_proj_workspace_bytes(nb_local, w_o.shape[1],
+                                                                    wo_splits)),
+                                dtype=torch.uint8, device=dev)
+        rec_events = []
+
+        def step(q_src, rows_src, ev=None):
+            if args.path == "fullkv":
+                ops.kv_append(k_rows, v_rows, k_cache, v_cache, tables, positions=positions)
+            else:
+                ops.latent_append(rows_src, x["cache"], tables, positions=positions)
+                rev = None
+                if ev is not None:
+                    rev = (torch.cuda.Event(enable_timing=True),
+                           torch.cuda.Event(enable_timing=True))
+                    rec_events.append(rev)
+                    rev[0].record()
+                ops.reconstruct_kv(x["cache"], x["w_k"], x["w_v"], slots=act_slots,
+                                   block_size=bs, k_out=k_cache, v_out=v_cache)
+                if rev is not None:
+                    rev[1].record()
+            if ev is not None:
+                ev[0].record()
+            ops.fullkv_decode(q_src, k_cache, v_cache, tables, lens, plan, scale=s.scale,
+                              out=ctx, workspace=fws)
+            if ev is not None:
+                ev[1].record()
+            res = ctx
+            if w_o is not None:
+                res = ops.out_proj(res.reshape(nb_local, -1), w_o, out=out, k_splits=wo_splits,
+                                   workspace=wo_ws)
+            return res
+
+        q_buf, rows_buf = q_in, new_rows
+
+        def run_step(ev=None):
+            return step(q_buf, rows_buf, ev)
+
+        # append, (reconstruction), full-KV partial + combine, W_o GEMM + reduction
+        launches_per_step = 3 + (args.path == "materialised") + (2 if w_o is not None else 0)
     else:
         plan = (ops.plan_workers(lens_host, s.block_size, device=dev) if mode == "tc"
                 else ops.plan_splits(lens_host, s.block_size, device=dev))
@@ -520,29 +594,46 @@ def run_ours(args, s, rank: int, world: int):
     if rank != 0:
         return None
     peaks, peak_kind = load_peaks()
-    algo = wl.algorithmic_bytes(s, attended_global, with_out_proj=w_o is not None)
+    algo = wl.algorithmic_bytes(s, attended_global, with_out_proj=w_o is not None,
+                                fullkv=args.path == "fullkv")
     value = algo / (ms_per_step * 1e-3) / 1e12
     # Roofline of the dominant kernel (split-K partial pass on rank 0):
     # latent rows attended x L x 2 bytes + query + table entries, per launch.
     toks_local = int(np.sum(attended, dtype=np.int64))
-    kern_bytes = (toks_local * s.latent_dim * 2 + nb_local * s.q_heads * s.latent_dim * 4
-                  + int(np.sum((attended + s.block_size - 1) // s.block_size)) * 4)
+    tables_bytes = int(np.sum((attended + s.block_size - 1) // s.block_size)) * 4
+    if args.path == "latent":
+        kern_bytes = (toks_local * s.latent_dim * 2 + nb_local * s.q_heads * s.latent_dim * 4
+                      + tables_bytes)
+        kern_name = f"latent partial ({mode})"
+        traffic = profiled_traffic(mode, s, toks_local)
+    else:
+        # full-KV decode (partial + combine): K and V rows attended + query + tables
+        kern_bytes = (toks_local * s.kv_heads * D * 2 * 2 + nb_local * s.q_heads * D * 4
+                      + tables_bytes)
+        kern_name = "full-KV decode (partial + combine)"
+        traffic = None
     hbm_peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
-    traffic = profiled_traffic(mode, s, toks_local)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                "frac": achieved / hbm_peak, "traffic": traffic, "kernel": f"latent partial ({mode})",
+                "frac": achieved / hbm_peak, "traffic": traffic, "kernel": kern_name,
                 "kernel_ms": kern_ms, "bytes_per_launch": kern_bytes,
                 "peak_source": f"{peak_kind} hbm_gbs"}
     flops = wl.algorithmic_flops(s, attended, with_out_proj=False)
-    roofline["achieved_tflops"] = flops / (kern_ms * 1e-3) / 1e12
+    if args.path == "latent":
+        roofline["achieved_tflops"] = flops / (kern_ms * 1e-3) / 1e12
+    path_info = {"path": args.path}
+    if args.path == "materialised" and rec_events:
+        rec_ms = statistics.mean(a.elapsed_time(b) for a, b in rec_events)
+        rec_flops = 2 * toks_local * s.kv_heads * D * (s.latent_dim + s.value_dim)
+        path_info.update(reconstruct_ms=rec_ms,
+                         reconstruct_tflops_fp32=rec_flops / (rec_ms * 1e-3) / 1e12)
     line = {"metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "us_per_step": ms_per_step * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": "f32" if mode == "exact" else "f16",
             "data": "synthetic (seeded, device-generated)",
-            "config": {"workload": s.name, "mode": mode, "batch": s.batch,
+            "config": {"workload": s.name, "mode": mode, **path_info, "batch": s.batch,
                        "q_heads": s.q_heads, "latent_dim": s.latent_dim,
                        "value_dim": s.value_dim, "head_dim": D, "block_size": s.block_size,
                        "tokens": int(attended_global.sum()), "w_o": w_o is not None,

@@ -98,6 +98,26 @@ int plkv_latent_append_slots_f16(const float* rows, const int64_t* slots, int64_
                                  uint16_t* cache, int64_t num_slots, int32_t latent_dim,
                                  int32_t* err_flags, plkv_stream_t stream);
 
+/* Materialised K / V from latent rows (replaces reconstruct_latent_kv_f32,
+ * lib.rs:517-580; reconstruct_latent_kv, latent_kv_reconstruction.rs:4-28;
+ * latent_kv_reconstruction_ref, attention_ref.py:227-274):
+ *   K[row, kv, d] = sum_{l < latent_dim} latent[row, l] * w_k[kv, l, d]
+ *   V[row, kv, d] = sum_{l < value_dim}  latent[row, l] * w_v[kv, l, d]
+ * FP32 accumulation.  latent: [num_slots, latent_dim] FP32 or FP16
+ * (latent_is_f16); rows: the slots listed in slots[n_rows] (NULL: slots
+ * 0 .. n_rows-1; negative slots are skipped); w_k / w_v head-major
+ * [kv_heads, latent_dim | value_dim, head_dim] FP32.  K / V are written at the
+ * same slot in the head-major paged layout [num_slots / block_size, kv_heads,
+ * block_size, head_dim], FP32 or FP16 (out_is_f16); block_size 1 gives the
+ * reference's token-major [row, kv_heads, head_dim].  Non-finite inputs or
+ * results raise PLKV_FLAG_NON_FINITE_INPUT, FP16 overflow
+ * PLKV_FLAG_FP16_OVERFLOW, slots >= num_slots PLKV_FLAG_BAD_POSITION. */
+int plkv_reconstruct_kv(const void* latent, int32_t latent_is_f16, int64_t num_slots,
+                        int32_t latent_dim, int32_t value_dim, const int64_t* slots,
+                        int64_t n_rows, const float* w_k, const float* w_v, int32_t kv_heads,
+                        int32_t head_dim, int32_t block_size, void* k_out, void* v_out,
+                        int32_t out_is_f16, int32_t* err_flags, plkv_stream_t stream);
+
 /* Device-side allocation of new token positions (replaces the bump allocator
  * PagedBlockTable.allocate_token_positions, block_table.py:26-38, and
  * BlockTable::allocate_tokens, lib.rs:1346-1364, for a batch on the GPU).

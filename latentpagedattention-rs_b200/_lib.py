@@ -77,6 +77,8 @@ SIGNATURES = {
     "plkv_latent_append_f16": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _I64, _P, _I64, _I32,
                                               _I32, _P, _P]),
     "plkv_latent_append_slots_f16": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _I32, _P, _P]),
+    "plkv_reconstruct_kv": (ctypes.c_int, [_P, _I32, _I64, _I32, _I32, _P, _I64, _P, _P, _I32,
+                                            _I32, _I32, _P, _P, _I32, _P, _P]),
     "plkv_allocate_slots": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _I64, _P, _I64, _P,
                                             _P]),
     "plkv_kv_append_f16": (ctypes.c_int, [_P, _P, _P, _I64, _P, _P, _P, _I64, _P, _P, _I64, _I32,

@@ -514,6 +514,102 @@ def out_proj(x: torch.Tensor, w_o: torch.Tensor, *, out: torch.Tensor | None = N
     return out
 
 
+# ------------------------------------------------- materialised reconstruction
+
+def reconstruct_kv(latent: torch.Tensor, w_k: torch.Tensor, w_v: torch.Tensor, *,
+                   slots: torch.Tensor | None = None, n_rows: int | None = None,
+                   block_size: int = 1, value_dim: int | None = None,
+                   out_dtype: torch.dtype = torch.float16, k_out: torch.Tensor | None = None,
+                   v_out: torch.Tensor | None = None,
+                   flags: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Materialised K / V from latent rows (reconstruct_latent_kv_f32,
+    lib.rs:517-580) into the head-major paged layout
+    ``[num_slots // block_size, KV, block_size, D]``.
+
+    ``latent`` is the latent pool viewed as rows ``[num_slots, L]`` (FP32 or
+    FP16; a paged cache ``[P, bs, L]`` is accepted as is); ``w_k`` / ``w_v``
+    head-major ``[KV, L, D]`` / ``[KV, Lv, D]`` FP32; ``slots`` (int64) picks
+    the rows to rebuild (default: the first ``n_rows``, else all)."""
+    if latent.dtype not in (torch.float32, torch.float16):
+        raise TypeError("latent must be FP32 or FP16")
+    _need_cuda("latent", latent)
+    _need_cuda("w_k", w_k, torch.float32)
+    _need_cuda("w_v", w_v, torch.float32)
+    L = latent.shape[-1]
+    rows = latent.reshape(-1, L)
+    num_slots = rows.shape[0]
+    KV, L2, D = w_k.shape
+    if L2 != L:
+        raise ValueError("latent_dim mismatch between latent rows and W_k")
+    Lv = w_v.shape[1] if value_dim is None else int(value_dim)
+    if tuple(w_v.shape) != (KV, Lv, D):
+        raise ValueError("W_v must be [kv_heads, value_dim, head_dim]")
+    if out_dtype not in (torch.float32, torch.float16):
+        raise TypeError("out_dtype must be FP32 or FP16")
+    if num_slots % block_size:
+        raise ValueError("the number of latent rows must be a multiple of block_size")
+    shape = (num_slots // block_size, KV, block_size, D)
+    if k_out is None:
+        k_out = torch.empty(shape, dtype=out_dtype, device=latent.device)
+    if v_out is None:
+        v_out = torch.empty(shape, dtype=out_dtype, device=latent.device)
+    for name, t in (("k_out", k_out), ("v_out", v_out)):
+        _need_cuda(name, t, out_dtype)
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{name} must have shape {shape}")
+    if slots is not None:
+        _need_cuda("slots", slots, torch.int64)
+        n = slots.numel() if n_rows is None else int(n_rows)
+        if n > slots.numel():
+            raise ValueError("n_rows exceeds the slot list")
+    else:
+        n = num_slots if n_rows is None else int(n_rows)
+    check(lib().plkv_reconstruct_kv(_ptr(rows), int(rows.dtype == torch.float16), num_slots, L,
+                                    Lv, _ptr(slots), n, _ptr(w_k), _ptr(w_v), KV, D, block_size,
+                                    _ptr(k_out), _ptr(v_out), int(out_dtype == torch.float16),
+                                    _ptr(flags), _stream(latent.device)), "plkv_reconstruct_kv")
+    return k_out, v_out
+
+
+def latent_kv_reconstruction(latent_cache, k_proj, v_proj, *, kv_heads: int,
+                             head_dim: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Drop-in for latent_kv_reconstruction_ref (attention_ref.py:227-274) on
+    the GPU: ``latent_cache [batch, seq, latent]``, ``k_proj`` / ``v_proj``
+    ``[latent, kv_heads * head_dim]`` -> K, V ``[batch, seq, kv_heads,
+    head_dim]`` FP32, with the reference's argument checks and messages."""
+    dev = torch.device("cuda")
+    lat = _to_cuda(latent_cache, torch.float32, dev)
+    kp = _to_cuda(k_proj, torch.float32, dev)
+    vp = _to_cuda(v_proj, torch.float32, dev)
+    if lat.ndim != 3:
+        raise ValueError("latent_cache must have shape [batch, seq_len, latent_dim]")
+    if kp.ndim != 2 or vp.ndim != 2:
+        raise ValueError("k_proj and v_proj must have shape [latent_dim, kv_heads * head_dim]")
+    if kp.shape != vp.shape:
+        raise ValueError("k_proj and v_proj shapes must match")
+    if kv_heads <= 0:
+        raise ValueError(f"kv_heads must be > 0, got {kv_heads}")
+    if head_dim <= 0:
+        raise ValueError(f"head_dim must be > 0, got {head_dim}")
+    batch, seq_len, latent_dim = lat.shape
+    if batch <= 0 or seq_len <= 0 or latent_dim <= 0:
+        raise ValueError("latent_cache dimensions must be > 0")
+    if kp.shape[0] != latent_dim:
+        raise ValueError("latent_dim mismatch between cache and projections")
+    if kp.shape[1] != kv_heads * head_dim:
+        raise ValueError("projection width must equal kv_heads * head_dim")
+    flags = _flags_tensor(dev)
+    k, v = reconstruct_kv(lat, projection_to_head_major(kp, kv_heads, head_dim),
+                          projection_to_head_major(vp, kv_heads, head_dim), block_size=1,
+                          out_dtype=torch.float32, flags=flags)
+    f = int(flags.item())
+    if f & (_lib.FLAG_NON_FINITE_INPUT | _lib.FLAG_FP16_OVERFLOW):
+        raise ValueError("reconstructed K cache must be finite")
+    raise_for_flags(f, "latent_kv_reconstruction")
+    return (k.reshape(batch, seq_len, kv_heads, head_dim),
+            v.reshape(batch, seq_len, kv_heads, head_dim))
+
+
 # ------------------------------------------- drop-ins for attention_ref.py
 
 def _check_group(q_heads: int, kv_heads: int, group_size: int) -> None:

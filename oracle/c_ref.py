@@ -71,6 +71,7 @@ def lib() -> ctypes.CDLL:
             "plkv_or_fullkv_decode_batch": (_INT, [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P,
                                                    _I64, _I64, _F, _P, _INT, _INT]),
             "plkv_or_out_proj": (_INT, [_P, _P, _I64, _I64, _I64, _P, _INT, _INT]),
+            "plkv_or_reconstruct_kv": (_INT, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _INT]),
             "plkv_or_max_threads": (_INT, []),
         }
         for name, (res, args) in sig.items():
@@ -242,6 +243,21 @@ def out_proj(x, w, acc64: bool = False, threads: int = 0) -> np.ndarray:
     _check(lib().plkv_or_out_proj(_ptr(xx), _ptr(ww), B, K, N, _ptr(out), int(acc64), threads),
            "out_proj")
     return out
+
+
+def reconstruct_kv(latent, w_k, w_v, acc64: bool = False) -> tuple[np.ndarray, np.ndarray]:
+    """lib.rs:517-580: token-major K, V [T, width] from latent rows [T, L],
+    w_k [L, width], w_v [Lv, width] (canonical)."""
+    lat = _c(latent, np.float32)
+    wk = _c(w_k, np.float32)
+    wv = _c(w_v, np.float32)
+    T, L = lat.shape
+    W = wk.shape[1]
+    k = np.zeros((T, W), np.float32)
+    v = np.zeros((T, W), np.float32)
+    _check(lib().plkv_or_reconstruct_kv(_ptr(lat), T, L, wv.shape[0], _ptr(wk), _ptr(wv), W,
+                                        _ptr(k), _ptr(v), int(acc64)), "reconstruct_kv")
+    return k, v
 
 
 def max_threads() -> int:

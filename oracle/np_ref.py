@@ -109,6 +109,41 @@ def paged_kv_write_ref(k_cache: np.ndarray, v_cache: np.ndarray, block_table: np
     return k_out, v_out
 
 
+# ------------------------------------------------- materialised reconstruction
+
+def latent_kv_reconstruction_ref(latent_cache: np.ndarray, k_proj: np.ndarray,
+                                 v_proj: np.ndarray, *, kv_heads: int,
+                                 head_dim: int) -> tuple[np.ndarray, np.ndarray]:
+    """attention_ref.py:227-274 -- K, V [batch, seq, kv_heads, head_dim] from a
+    latent cache [batch, seq, latent] and projections [latent, kv_heads*head_dim]."""
+    if latent_cache.ndim != 3:
+        raise ValueError("latent_cache must have shape [batch, seq_len, latent_dim]")
+    if k_proj.ndim != 2 or v_proj.ndim != 2:
+        raise ValueError("k_proj and v_proj must have shape [latent_dim, kv_heads * head_dim]")
+    if k_proj.shape != v_proj.shape:
+        raise ValueError("k_proj and v_proj shapes must match")
+    if kv_heads <= 0:
+        raise ValueError(f"kv_heads must be > 0, got {kv_heads}")
+    if head_dim <= 0:
+        raise ValueError(f"head_dim must be > 0, got {head_dim}")
+    batch, seq_len, latent_dim = latent_cache.shape
+    if batch <= 0 or seq_len <= 0 or latent_dim <= 0:
+        raise ValueError("latent_cache dimensions must be > 0")
+    if k_proj.shape[0] != latent_dim:
+        raise ValueError("latent_dim mismatch between cache and projections")
+    if k_proj.shape[1] != kv_heads * head_dim:
+        raise ValueError("projection width must equal kv_heads * head_dim")
+    k = np.asarray(latent_cache @ k_proj, dtype=np.float32).reshape(batch, seq_len, kv_heads,
+                                                                      head_dim)
+    v = np.asarray(latent_cache @ v_proj, dtype=np.float32).reshape(batch, seq_len, kv_heads,
+                                                                      head_dim)
+    if not np.all(np.isfinite(k)):
+        raise ValueError("reconstructed K cache must be finite")
+    if not np.all(np.isfinite(v)):
+        raise ValueError("reconstructed V cache must be finite")
+    return k, v
+
+
 # ------------------------------------------------------------ block_table.py
 
 class PagedBlockTable:
@@ -408,6 +443,41 @@ def fullkv_decode_batch_f64(q, k_f16, v_f16, tables, lens, block_size, scale, gr
         probs.append(p)
         ctx[b] = np.einsum("ht,htd->hd", p, vh)
     return scores, probs, ctx
+
+
+# ------------------------------------------------- materialised reconstruction
+
+def latent_kv_reconstruction_ref(latent_cache: np.ndarray, k_proj: np.ndarray,
+                                 v_proj: np.ndarray, *, kv_heads: int,
+                                 head_dim: int) -> tuple[np.ndarray, np.ndarray]:
+    """attention_ref.py:227-274 -- K, V [batch, seq, kv_heads, head_dim] from a
+    latent cache [batch, seq, latent] and projections [latent, kv_heads*head_dim]."""
+    if latent_cache.ndim != 3:
+        raise ValueError("latent_cache must have shape [batch, seq_len, latent_dim]")
+    if k_proj.ndim != 2 or v_proj.ndim != 2:
+        raise ValueError("k_proj and v_proj must have shape [latent_dim, kv_heads * head_dim]")
+    if k_proj.shape != v_proj.shape:
+        raise ValueError("k_proj and v_proj shapes must match")
+    if kv_heads <= 0:
+        raise ValueError(f"kv_heads must be > 0, got {kv_heads}")
+    if head_dim <= 0:
+        raise ValueError(f"head_dim must be > 0, got {head_dim}")
+    batch, seq_len, latent_dim = latent_cache.shape
+    if batch <= 0 or seq_len <= 0 or latent_dim <= 0:
+        raise ValueError("latent_cache dimensions must be > 0")
+    if k_proj.shape[0] != latent_dim:
+        raise ValueError("latent_dim mismatch between cache and projections")
+    if k_proj.shape[1] != kv_heads * head_dim:
+        raise ValueError("projection width must equal kv_heads * head_dim")
+    k = np.asarray(latent_cache @ k_proj, dtype=np.float32).reshape(batch, seq_len, kv_heads,
+                                                                      head_dim)
+    v = np.asarray(latent_cache @ v_proj, dtype=np.float32).reshape(batch, seq_len, kv_heads,
+                                                                      head_dim)
+    if not np.all(np.isfinite(k)):
+        raise ValueError("reconstructed K cache must be finite")
+    if not np.all(np.isfinite(v)):
+        raise ValueError("reconstructed V cache must be finite")
+    return k, v
 
 
 # ------------------------------------------------------------ block_table.py

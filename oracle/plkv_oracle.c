@@ -30,6 +30,8 @@
  *   plkv_or_fullkv_decode_batch  same for the full-KV baseline
  *   plkv_or_out_proj             W_o output projection (extension; plain
  *                                matrix product)
+ *   plkv_or_reconstruct_kv       lib.rs:517-580 (reconstruct_latent_kv_f32):
+ *                                materialised K / V from latent rows
  *
  * Status codes are the PLKV_* values of include/plkv_b200.h.
  */
@@ -495,6 +497,53 @@ int plkv_or_out_proj(const float* x, const float* w, int64_t batch, int64_t in_d
             }
             memcpy(out + b * out_dim, acc, (size_t)out_dim * sizeof(float));
             free(acc);
+        }
+    }
+    return OR_OK;
+}
+
+/* lib.rs:517-580: K[t, n] = sum_l latent[t, l] * w_k[l, n] over l < latent_dim
+ * and V[t, n] = sum_l latent[t, l] * w_v[l, n] over l < value_dim (the
+ * reference uses value_dim = latent_dim), n < width = kv_heads * head_dim,
+ * token-major outputs.  The reference's loop order and FP32 accumulation
+ * (product rounded, then the sum); acc64 accumulates in FP64 instead.
+ * Rejects non-finite inputs and non-finite results like the reference. */
+int plkv_or_reconstruct_kv(const float* latent, int64_t seq_len, int64_t latent_dim,
+                           int64_t value_dim, const float* w_k, const float* w_v, int64_t width,
+                           float* k_out, float* v_out, int acc64) {
+    if (seq_len <= 0 || latent_dim <= 0 || value_dim <= 0 || width <= 0) return OR_ZERO_VALUE;
+    if (value_dim > latent_dim) return OR_INVALID_ARGUMENT;
+    for (int64_t i = 0; i < seq_len * latent_dim; ++i)
+        if (!isfinite(latent[i])) return OR_NON_FINITE;
+    for (int64_t i = 0; i < latent_dim * width; ++i)
+        if (!isfinite(w_k[i])) return OR_NON_FINITE;
+    for (int64_t i = 0; i < value_dim * width; ++i)
+        if (!isfinite(w_v[i])) return OR_NON_FINITE;
+    for (int64_t t = 0; t < seq_len; ++t) {
+        const float* row = latent + t * latent_dim;
+        for (int64_t n = 0; n < width; ++n) {
+            float k_sum, v_sum;
+            if (acc64) {
+                double k = 0.0, v = 0.0;
+                for (int64_t l = 0; l < latent_dim; ++l) k += (double)row[l] * w_k[l * width + n];
+                for (int64_t l = 0; l < value_dim; ++l) v += (double)row[l] * w_v[l * width + n];
+                k_sum = (float)k;
+                v_sum = (float)v;
+            } else {
+                k_sum = 0.0f;
+                v_sum = 0.0f;
+                for (int64_t l = 0; l < latent_dim; ++l) {
+                    float p = row[l] * w_k[l * width + n];
+                    k_sum += p;
+                    if (l < value_dim) {
+                        float q = row[l] * w_v[l * width + n];
+                        v_sum += q;
+                    }
+                }
+            }
+            if (!isfinite(k_sum) || !isfinite(v_sum)) return OR_NON_FINITE;
+            k_out[t * width + n] = k_sum;
+            v_out[t * width + n] = v_sum;
         }
     }
     return OR_OK;

@@ -48,6 +48,7 @@ REFERENCE_FIXTURES = [
     "block_table_seq5_block2.json",
     "block_table_seq128_block16.json",
     "paged_lookup_f32_seq5_block2_width4.json",
+    "latent_kv_reconstruction_f32.json",
 ]
 
 
@@ -103,6 +104,7 @@ def write_reference_fixtures(fx, ref_root: str, out_dir: str) -> None:
         "block_table_seq5_block2.json": lambda: fx.block_table_fixture(5, 2),
         "block_table_seq128_block16.json": lambda: fx.block_table_fixture(128, 16),
         "paged_lookup_f32_seq5_block2_width4.json": fx.paged_lookup_f32_fixture,
+        "latent_kv_reconstruction_f32.json": fx.latent_kv_reconstruction_f32_fixture,
     }
     drift = {}
     for name in REFERENCE_FIXTURES:

@@ -325,3 +325,56 @@ def test_model_shaped_golden(pkg):
     assert_close(sc, d["scores"], SCORE_TOL, "scores")
     assert_close(p, d["probs"], PROB_TOL, "probs")
     assert_close(ctx, d["ctx"], CTX_TOL, "ctx")
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_reconstruction_fixture(case):
+    """latent_kv_reconstruction_f32.json: the C restatement of
+    reconstruct_latent_kv_f32 (lib.rs:517-580) and the NumPy restatement of
+    latent_kv_reconstruction_ref (attention_ref.py:227-274) at the reference's
+    CPU tolerances (latent_kv_reconstruction_gpu.rs:10-11: 1e-5 / 1e-5)."""
+    from oracle import np_ref
+
+    fx = load_reference_fixture("latent_kv_reconstruction_f32.json")
+    c = fx["cases"][case]
+    KV, D = fx["kv_heads"], fx["head_dim"]
+    lat = np.asarray(c["latent_cache"], np.float32)
+    kp = np.asarray(c["k_projection"], np.float32)
+    vp = np.asarray(c["v_projection"], np.float32)
+    ek = np.asarray(c["expected_k_token_major"], np.float32)
+    ev = np.asarray(c["expected_v_token_major"], np.float32)
+    k, v = c_ref.reconstruct_kv(lat, kp, vp)
+    for got, exp in ((k, ek), (v, ev)):
+        np.testing.assert_allclose(got.reshape(exp.shape), exp, rtol=1e-5, atol=1e-5)
+    k_hm = k.reshape(-1, KV, D).transpose(1, 0, 2)
+    np.testing.assert_allclose(k_hm, np.asarray(c["expected_k_head_major"]), rtol=1e-5, atol=1e-5)
+    nk, nv = np_ref.latent_kv_reconstruction_ref(lat[None], kp, vp, kv_heads=KV, head_dim=D)
+    np.testing.assert_allclose(nk[0], ek, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(nv[0], ev, rtol=1e-5, atol=1e-5)
+
+
+def test_reconstruction_rejections():
+    """lib.rs:2156-2176 and attention_ref.py:246-272: bad shapes and
+    non-finite inputs are rejected."""
+    from oracle import np_ref
+
+    lat = np.zeros((8, 8), np.float32)
+    proj = np.zeros((8, 16), np.float32)
+    bad = lat.copy()
+    bad[0, 0] = np.nan
+    with pytest.raises(RuntimeError):
+        c_ref.reconstruct_kv(bad, proj, proj)
+    with pytest.raises(ValueError):
+        np_ref.latent_kv_reconstruction_ref(lat, proj, proj, kv_heads=2, head_dim=8)
+    with pytest.raises(ValueError):
+        np_ref.latent_kv_reconstruction_ref(lat[None], proj[:, :15], proj[:, :15], kv_heads=2,
+                                            head_dim=8)
+    with pytest.raises(ValueError):
+        np_ref.latent_kv_reconstruction_ref(lat[None], proj, proj[:, :8], kv_heads=2, head_dim=8)
+    with pytest.raises(ValueError):
+        np_ref.latent_kv_reconstruction_ref(lat[None], proj, proj, kv_heads=0, head_dim=8)
+    huge = np.full((1, 1, 8), 3e38, np.float32)
+    with pytest.raises(ValueError):
+        np_ref.latent_kv_reconstruction_ref(huge, np.full((8, 16), 3e38, np.float32),
+                                            np.full((8, 16), 3e38, np.float32), kv_heads=2,
+                                            head_dim=8)
