@@ -12,7 +12,8 @@
 // Work split.  A cluster of two CTAs (a tcgen05 CTA pair) is persistent: it
 // processes the items of one worker of plkv_plan_workers (or one item) in
 // tiles of 64 tokens.  CTA r owns query heads [64r, 64r+64).
-//   S = Q . L^T  : cta_group::2 MMA, M = 128 heads, N = 64 tokens, K = 576.
+//   S = Q . L^T  : cta_group::2 MMA, M = 128 heads, N = 64 tokens, K = 576
+//                  (four partials of K = 144, see below).
 //                  CTA r supplies its heads' Q and tokens [32r, 32r+32) of L;
 //                  its TMEM receives its 64 heads x 64 tokens (32 columns).
 //   O += P . V   : cta_group::2 MMA, M = 128 heads, N = 256 value columns
@@ -35,10 +36,19 @@
 // = head, and the two threads sharing a head (token halves) agree through
 // shared memory, so the CTAs never exchange softmax state.
 //
+// MMA issue is split over four threads of the leader CTA.  One thread issues
+// a tcgen05.mma every ~60 cycles however small the MMA is, and at N = 64 the
+// tensor pipe finishes one in less; measured on B200, 36 pair MMAs take 1.52
+// us from one issuing warp, 0.83 us from two and 0.49 us from four.  So S is
+// cut along K into four 9-step partials, each accumulated by its own issuer
+// in its own TMEM columns and added by the softmax threads; issuers 0 and 1
+// also issue the two 256-column halves of O.  Barriers completed by MMA
+// commits count one arrival per issuer that commits to them.
+//
 // Warp roles per CTA: 0 = Q and K loads, 1 = TMEM allocation and (leader CTA)
-// MMA issue, 2 = V loads, 4..7 = softmax and epilogue.  Every barrier wait is
-// bounded (1 s): on expiry the kernel records PLKV_FLAG_TIMEOUT, abandons its
-// work, releases tensor memory and exits.
+// MMA issue, 2 = V loads, 3, 8, 9 = (leader CTA) MMA issue, 4..7 = softmax and
+// epilogue.  Every barrier wait is bounded (1 s): on expiry the kernel records
+// PLKV_FLAG_TIMEOUT, abandons its work, releases tensor memory and exits.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -72,8 +82,12 @@ constexpr uint32_t kQTx = 2u * kQBytes;                       // both CTAs
 constexpr uint32_t kKTx = 2u * kKStage;                       // both CTAs
 constexpr uint32_t kVTx = kVStage;                            // own CTA
 constexpr uint32_t kTmemCols = 512;
-constexpr int kSBufs = 4;                                     // S accumulators in TMEM
-constexpr uint32_t kTmemO = 32 * kSBufs;                      // S buffers at 0, 32, 64, 96
+constexpr int kSBufs = 2;                                     // S accumulators in TMEM
+constexpr uint32_t kTmemO = 0;                                // O at 0..255
+constexpr int kIssuers = 4;                                   // MMA-issuing threads (warps 1, 3, 8, 9)
+constexpr int kKPer = 36 / kIssuers;                          // S k-steps per issuer
+// S partial p of buffer sb at 256 + 32 (kSBufs p + sb)
+__host__ __device__ constexpr uint32_t s_col(int p, int sb) { return 256u + 32u * (kSBufs * p + sb); }
 constexpr float kTau = 8.f;
 constexpr int kPrefetchTiles = 6;                             // L2 prefetch distance
 constexpr float kLn2 = 0.6931471805599453f;
@@ -155,7 +169,7 @@ __device__ __forceinline__ int half_row(const ItemGeom& g, int j, int h,
     return phys * bs + (hs - lb * bs);
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
 latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                          const __grid_constant__ CUtensorMap q_map,
                          const uint16_t* __restrict__ cache, int bs,
@@ -187,17 +201,17 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
 
     if (tid == 0) {
         mbar_init(mb + kBarQFull, 1);
-        mbar_init(mb + kBarQFree, 1);
+        mbar_init(mb + kBarQFree, kIssuers);
         mbar_init(mb + kBarOFree, 2);
         for (int i = 0; i < 2; ++i) {
             mbar_init(mb + kBarKFull + 8 * i, 1);
-            mbar_init(mb + kBarKEmpty + 8 * i, 1);
+            mbar_init(mb + kBarKEmpty + 8 * i, kIssuers);
             mbar_init(mb + kBarVFull + 8 * i, 1);
-            mbar_init(mb + kBarVEmpty + 8 * i, 1);
+            mbar_init(mb + kBarVEmpty + 8 * i, 2);
             mbar_init(mb + kBarPFull + 8 * i, 2);
-            mbar_init(mb + kBarODone + 8 * i, 1);
+            mbar_init(mb + kBarODone + 8 * i, 2);
         }
-        for (int i = 0; i < kSBufs; ++i) mbar_init(mb + kBarSFull + 8 * i, 1);
+        for (int i = 0; i < kSBufs; ++i) mbar_init(mb + kBarSFull + 8 * i, kIssuers);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -297,16 +311,19 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
             }
         }
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp == 3 || warp == 8 || warp == 9) {
         // ---------------------------------------------- MMA issue (leader)
-        // One thread schedules both MMAs without blocking: S(g) as soon as K
-        // tile g landed and one of the kSBufs S accumulators is free (its
-        // previous tile's O was issued, so its softmax is done), O(g) as soon
-        // as P(g) is ready.  S work thus stays queued on the tensor pipe while
-        // the softmax of earlier tiles runs.  S never crosses into the next
-        // item before that item's Q is loaded, which waits for every MMA of
-        // the current item (barrier QFree).
+        // Each issuer schedules its MMAs without blocking: its S partial of
+        // tile g as soon as K tile g landed and S buffer g % kSBufs is free
+        // (P of its previous tile was written, so the softmax read it), and,
+        // for issuers 0 and 1, its O half of tile g as soon as P(g) is ready.
+        // S work thus stays queued on the tensor pipe while the softmax of
+        // earlier tiles runs.  S never crosses into the next item before that
+        // item's Q is loaded, which waits until every issuer's S of the
+        // current item completed (barrier QFree).
         if (leader && lane == 0) {
+            const int part = warp == 1 ? 0 : warp == 3 ? 1 : warp == 8 ? 2 : 3;
+            const bool has_o = part < 2;  // parts 0 and 1 also issue O half `part`
             const uint32_t id_s = idesc_f16(128, 64, false, false);
             const uint32_t id_o = idesc_f16(128, 256, false, true);
             const int n_items_w = i_end - i_begin;
@@ -317,7 +334,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                                         : ItemGeom{0, 0, 0, 0};
             ItemGeom go = gs;
             uint64_t idle_since = 0, next_check = 0;
-            while (oi < n_items_w) {
+            while (has_o ? oi < n_items_w : si < n_items_w) {
                 bool did = false;
                 if (si < n_items_w) {
                     if (!s_q && mbar_try_wait(mb + kBarQFull, si & 1)) {
@@ -326,23 +343,28 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                     }
                     if (s_q) {
                         if (sj >= gs.n_tiles) {
+                            mma_commit_pair(mb + kBarQFree, 0x3);  // every S of item si issued
                             if (++si < n_items_w)
                                 gs = item_geom(items, i_begin + si, seq_lens, bs, cap, flags, false);
                             sj = 0;
                             s_q = false;
                             did = true;
-                        } else if (sg < og + kSBufs &&
+                        } else if ((sg < kSBufs ||
+                                    mbar_try_wait(mb + kBarPFull + 8 * ((sg - kSBufs) & 1),
+                                                  ((sg - kSBufs) >> 1) & 1)) &&
                                    mbar_try_wait(mb + kBarKFull + 8 * (sg & 1), (sg >> 1) & 1)) {
                             tc_fence_after();
                             const int st = sg & 1, sb = sg % kSBufs;
                             const uint32_t kreg = sbase + kKOff + st * kKStage;
-#pragma unroll 4
-                            for (int k = 0; k < kKBlocks * 4; ++k) {
+                            const int k0 = kKPer * part;
+                            const uint32_t dcol = s_col(part, sb);
+#pragma unroll
+                            for (int k = k0; k < k0 + kKPer; ++k) {
                                 const uint64_t a = sdesc_sw128(
                                     sbase + kQOff + (k >> 2) * kQAtom + (k & 3) * 32, 16, 1024);
                                 const uint64_t b =
                                     sdesc_sw128(kreg + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
-                                mma_pair_f16(tmem + 32 * sb, a, b, id_s, k > 0 ? 1u : 0u);
+                                mma_pair_f16(tmem + dcol, a, b, id_s, k > k0 ? 1u : 0u);
                             }
                             mma_commit_pair(mb + kBarSFull + 8 * sb, 0x3);
                             mma_commit_pair(mb + kBarKEmpty + 8 * st, 0x3);
@@ -352,8 +374,8 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                         }
                     }
                 }
-                if (oj >= go.n_tiles) {
-                    mma_commit_pair(mb + kBarQFree, 0x3);  // every MMA of item oi issued
+                if (!has_o) {
+                } else if (oj >= go.n_tiles) {
                     if (++oi < n_items_w)
                         go = item_geom(items, i_begin + oi, seq_lens, bs, cap, flags, false);
                     oj = 0;
@@ -364,8 +386,8 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                     const int st = og & 1;
                     const uint32_t vreg = sbase + kVOff + st * kVStage;
                     const uint32_t preg = sbase + kPOff + st * kPBytes;
-#pragma unroll
-                    for (int i = 0; i < 2; ++i)
+                    {
+                        const int i = part;
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
                             const uint64_t a = sdesc_sw128(preg + k * 32, 16, 1024);
@@ -375,6 +397,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                             mma_pair_f16(tmem + kTmemO + 128 * i, a, b, id_o,
                                          (oj > 0 || k > 0) ? 1u : 0u);
                         }
+                    }
                     mma_commit_pair(mb + kBarODone + 8 * st, 0x3);
                     mma_commit_pair(mb + kBarVEmpty + 8 * st, 0x3);
                     ++oj;
@@ -435,8 +458,20 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                 float s[32];
                 if (ok) {
                     tc_fence_after();
-                    tmem_ld32(tmem + lane_base + 32 * sb, s);
+                    float s1[32];
+                    tmem_ld32(tmem + lane_base + s_col(0, sb), s);
+                    tmem_ld32(tmem + lane_base + s_col(1, sb), s1);
                     tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) s[i] += s1[i];
+                    tmem_ld32(tmem + lane_base + s_col(2, sb), s1);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) s[i] += s1[i];
+                    tmem_ld32(tmem + lane_base + s_col(3, sb), s1);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) s[i] += s1[i];
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) s[i] = -INFINITY;
@@ -649,7 +684,7 @@ cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWor
         if (e != cudaSuccess) return e;
     }
     const int workers = (a.worker_item_begin && a.n_workers > 0) ? a.n_workers : a.n_items;
-    tc::latent_partial_tc_kernel<<<2 * workers, 256, tc::kSmemBytes, st>>>(
+    tc::latent_partial_tc_kernel<<<2 * workers, 320, tc::kSmemBytes, st>>>(
         cache_map, q_map, a.cache, a.block_size, a.block_tables, a.max_blocks, a.num_physical,
         a.seq_lens,
         a.items, (a.worker_item_begin && a.n_workers > 0) ? a.worker_item_begin : nullptr, ws,
