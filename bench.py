@@ -13,10 +13,12 @@ combine with the W_uv / W_v projection run; `--with-wo` adds the W_o output
 projection.  `--grow` makes every step append a new token per sequence
 instead: its position is allocated on the device (block table, length and
 pool counter advance there), as in the reference's write-then-attend loop.
-On one GPU the step is recorded once into a CUDA graph and replayed
-(`--no-graph` launches it eagerly); the partial pass's kernel time always
-comes from CUDA events around it in the eager steps that precede the replays.  The default workload is the long-context one (8 sequences of
-131072 tokens, absorbed-MLA shapes: 128 heads, latent 512 + 64, block 64).
+The step is recorded once into a CUDA graph and replayed, the NCCL
+all-gather of the split-K shards included (`--no-graph` launches it eagerly);
+the partial pass's kernel time always comes from CUDA events around it in the
+eager steps that precede the replays.  The default workload is the long-context
+one (8 sequences of 131072 tokens, absorbed-MLA shapes: 128 heads, latent
+512 + 64, block 64).
 
 Metric: achieved HBM TB/s = algorithmic bytes of the step / step time (the
 step time is reported as ms_per_step).  With N > 1 (torchrun) each sequence's
@@ -284,10 +286,9 @@ def run_ours(args, s, rank: int, world: int):
         mode = "tc" if (s.absorbed and ops.tc_available(s)) else "exact"
     split_k = world > 1 and s.name in SPLIT_K_WORKLOADS
     if args.graph is None:
-        # default: graphs wherever the step holds no collective
-        args.graph = not split_k
-    if split_k and (args.graph or args.grow):
-        raise SystemExit("--graph / --grow: not with the split-K shards of this workload")
+        args.graph = True
+    if split_k and args.grow:
+        raise SystemExit("--grow: not with the split-K shards of this workload")
     if args.path != "latent" and (s.absorbed or split_k or args.grow):
         raise SystemExit("--path fullkv / materialised: one-GPU GQA workloads with W_k, no --grow")
     D = s.head_dim
@@ -512,6 +513,7 @@ def run_ours(args, s, rank: int, world: int):
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
     elapsed_ms = eager_ms
     stepper = run_step
+    graph = None
     if args.graph:
         # The same step recorded once into a CUDA graph and replayed.
         if args.grow:
@@ -520,10 +522,14 @@ def run_ours(args, s, rank: int, world: int):
             def stepper():
                 return loop.step()[0]
         else:
+            # With split-K the step holds the NCCL all-gather of the shards'
+            # (context, lse); every rank captures the same sequence, after the
+            # eager steps above have set up the communicator.
             torch.cuda.synchronize(dev)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, capture_error_mode="thread_local"):
                 g_res = step(q_buf, rows_buf)
+            barrier()
 
             def stepper():
                 graph.replay()
@@ -591,6 +597,12 @@ def run_ours(args, s, rank: int, world: int):
         e2e = {"ms_per_step": e2e_ms, "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h)}
 
+    if graph is not None:
+        # A graph that holds NCCL calls must be released before the process
+        # group is destroyed.
+        torch.cuda.synchronize(dev)
+        graph.reset()
+        graph = None
     if rank != 0:
         return None
     peaks, peak_kind = load_peaks()
@@ -686,16 +698,27 @@ def main():
     import torch.distributed as dist
     from datetime import timedelta
 
+    saved_stdout = None
     if world > 1:
+        # Library banners (NCCL prints its version on rank 0) go to stderr, so
+        # that rank 0's standard output is the one JSON line.
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    line = None
     try:
         line = run_ours(args, s, rank, world)
-        if rank == 0 and line is not None:
-            print(json.dumps(line), flush=True)
     finally:
         if world > 1:
             dist.destroy_process_group()
+        if saved_stdout is not None:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

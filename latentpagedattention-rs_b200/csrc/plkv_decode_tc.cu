@@ -261,6 +261,9 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                                                           num_physical, bs, flags) * kLatent,
                                 32 * kLatent * 2);
                 for (int j = 0; ok && j < g.n_tiles; ++j) {
+                    // Block-table lookups first: their latency then overlaps
+                    // the wait for a free stage instead of following it.
+                    const int y = half_row(g, j, (int)rank, tables, max_blocks, num_physical, bs, flags);
                     if (j + kPrefetchTiles < g.n_tiles)
                         prefetch_l2(cache + (int64_t)half_row(g, j + kPrefetchTiles, (int)rank,
                                                               tables, max_blocks, num_physical, bs,
@@ -271,7 +274,6 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                     if (gj >= 2 && !(ok = mbar_wait(mb + kBarKEmpty + 8 * st, ((gj - 2) >> 1) & 1,
                                                     flags, abort_flag)))
                         break;
-                    const int y = half_row(g, j, (int)rank, tables, max_blocks, num_physical, bs, flags);
                     if (leader) mbar_arrive_expect_tx(mb + kBarKFull + 8 * st, kKTx);
                     const uint32_t dst = sbase + kKOff + st * kKStage;
                     const uint32_t fb = st ? kfull1 : kfull0;
@@ -293,11 +295,11 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                 const ItemGeom g = item_geom(items, ii, seq_lens, bs, cap, flags, false);
                 for (int j = 0; j < g.n_tiles; ++j) {
                     const int gj = gt + j, st = gj & 1;
+                    const int y0 = half_row(g, j, 0, tables, max_blocks, num_physical, bs, flags);
+                    const int y1 = half_row(g, j, 1, tables, max_blocks, num_physical, bs, flags);
                     if (gj >= 2 && !(ok = mbar_wait(mb + kBarVEmpty + 8 * st, ((gj - 2) >> 1) & 1,
                                                     flags, abort_flag)))
                         break;
-                    const int y0 = half_row(g, j, 0, tables, max_blocks, num_physical, bs, flags);
-                    const int y1 = half_row(g, j, 1, tables, max_blocks, num_physical, bs, flags);
                     mbar_arrive_expect_tx(mb + kBarVFull + 8 * st, kVTx);
                     const uint32_t dst = sbase + kVOff + st * kVStage;
                     for (int h = 0; h < 2; ++h)
