@@ -320,6 +320,15 @@ def run_ours(args, s, rank: int, world: int):
     else:
         positions = torch.as_tensor(gpos.astype(np.int32), device=dev)
     w_o = x.get("w_o")
+    # W_o column-sharded across ranks: this rank keeps out_dim / world columns.
+    wo_sharded = w_o is not None and world > 1
+    if wo_sharded:
+        if args.grow:
+            raise SystemExit("--with-wo on several GPUs: not with --grow")
+        c0, c1 = mg.column_range(s.out_dim, world, rank)
+        w_o = w_o[:, c0:c1].contiguous()
+        x["w_o"] = None
+        torch.cuda.empty_cache()
     if args.grow:
         lens0 = lens_host.astype(np.int64) - 1     # tokens stored before the first step
         cap = lens0 + grow_steps
@@ -427,17 +436,32 @@ def run_ours(args, s, rank: int, world: int):
                                    device=dev) if split_k else None
         gathered_lse = torch.empty((world, nb_local, s.q_heads), dtype=torch.float32,
                                    device=dev) if split_k else None
-        out = (torch.empty((nb_local, s.out_dim), dtype=torch.float32, device=dev)
-               if w_o is not None else None)
+        K_o = s.q_heads * D
+        if wo_sharded:
+            # rows projected on every rank: the merged contexts (split-K) or
+            # every rank's sequences, gathered into equal padded blocks
+            max_rows = (B if split_k else
+                        int(np.bincount(mg.lpt_assign(global_lens, world), minlength=world).max()))
+            proj_rows = B if split_k else world * max_rows
+            g_rows = (None if split_k else
+                      torch.zeros((world, max_rows, K_o), dtype=torch.float32, device=dev))
+            g_out = torch.empty((world, proj_rows, w_o.shape[1]), dtype=torch.float32, device=dev)
+            out = torch.empty((proj_rows, w_o.shape[1]), dtype=torch.float32, device=dev)
+        else:
+            out = (torch.empty((nb_local, s.out_dim), dtype=torch.float32, device=dev)
+                   if w_o is not None else None)
         q_lat_buf = (None if s.absorbed else
                      torch.empty((nb_local, s.q_heads, s.latent_dim), dtype=torch.float32,
                                  device=dev))
         wo_splits = wo_ws = None
         if w_o is not None:
             wo_splits = ops.default_out_proj_splits(w_o.shape[0], w_o.shape[1], dev)
-            wo_ws = torch.empty(max(1, ops.out_proj_workspace_bytes(nb_local, w_o.shape[1],
+            wo_ws = torch.empty(max(1, ops.out_proj_workspace_bytes(out.shape[0], w_o.shape[1],
                                                                     wo_splits)),
                                 dtype=torch.uint8, device=dev)
+
+        def project(a, w):
+            return ops.out_proj(a, w, out=out, k_splits=wo_splits, workspace=wo_ws)
 
         def step(q_src, rows_src, ev=None):
             if split_k:
@@ -462,9 +486,13 @@ def run_ours(args, s, rank: int, world: int):
                 res = mg.gather_and_merge(ctx, r["lse"], world,
                                           lambda c, l: ops.lse_merge(c, l)[0],
                                           gathered_ctx, gathered_lse)
-            if w_o is not None:
-                res = ops.out_proj(res.reshape(nb_local, -1), w_o, out=out, k_splits=wo_splits,
-                                   workspace=wo_ws)
+            if w_o is not None and wo_sharded:
+                rows = (res.reshape(B, -1) if split_k else
+                        mg.gather_rows(res.reshape(nb_local, -1), world, max_rows,
+                                       gathered=g_rows).reshape(-1, K_o))
+                res = mg.sharded_out_proj(rows, w_o, world, project, gathered=g_out)
+            elif w_o is not None:
+                res = project(res.reshape(nb_local, -1), w_o)
             return res
 
         q_buf, rows_buf = q_in, new_rows

@@ -11,6 +11,13 @@ Two partitionings, both strong scaling of one global batch:
 * sequence sharding: sequences go to ranks by longest-processing-time on
   their lengths (``lpt_assign``); no collective on the data path.
 
+With a W_o output projection, W_o is column-sharded: rank r holds columns
+``column_range(out_dim, world, r)``.  The rows to project (the merged
+contexts under split-K, every rank's sequences under sequence sharding,
+gathered with ``gather_rows``) are multiplied by the local slice and the
+column slices are all-gathered (``sharded_out_proj``): each rank reads 1/world
+of W_o instead of all of it.
+
 The functions take the decode / merge callables as arguments so that the
 same host logic runs with the CUDA kernels on GPUs and, in tests, with
 CPU stand-ins over a ``gloo`` process group.
@@ -84,3 +91,61 @@ def gather_and_merge(ctx, lse, world: int, merge_fn, gathered_ctx=None, gathered
         dist.all_gather(list(gathered_ctx.unbind(0)), ctx.contiguous(), group=group)
         dist.all_gather(list(gathered_lse.unbind(0)), lse.contiguous(), group=group)
     return merge_fn(gathered_ctx, gathered_lse)
+
+
+# ---------------------------------------------------- W_o column sharding
+
+def column_range(out_dim: int, world: int, rank: int) -> tuple[int, int]:
+    """Columns [c0, c1) of W_o that `rank` holds: equal contiguous slices
+    (``out_dim`` must be a multiple of ``world``)."""
+    if out_dim % world:
+        raise ValueError(f"out_dim {out_dim} is not a multiple of the world size {world}")
+    w = out_dim // world
+    return rank * w, (rank + 1) * w
+
+
+def gather_rows(x_local, world: int, max_rows: int, gathered=None, group=None):
+    """All-gather every rank's row block ``x_local [n_r, K]`` (n_r <= max_rows)
+    into ``gathered [world, max_rows, K]``; rows past n_r of a block are
+    left as they were (the caller ignores them)."""
+    import torch
+    import torch.distributed as dist
+
+    n, K = x_local.shape
+    if n > max_rows:
+        raise ValueError("x_local has more rows than max_rows")
+    if gathered is None:
+        gathered = torch.zeros((world, max_rows, K), dtype=x_local.dtype, device=x_local.device)
+    send = x_local
+    if n < max_rows:
+        send = torch.zeros((max_rows, K), dtype=x_local.dtype, device=x_local.device)
+        send[:n] = x_local
+    if x_local.device.type == "cuda":
+        dist.all_gather_into_tensor(gathered, send.contiguous(), group=group)
+    else:
+        dist.all_gather(list(gathered.unbind(0)), send.contiguous(), group=group)
+    return gathered
+
+
+def sharded_out_proj(x_full, w_o_slice, world: int, proj_fn, gathered=None, group=None):
+    """Column-sharded W_o: every rank computes ``x_full @ w_o_slice`` (its
+    ``out_dim / world`` columns, ``proj_fn(x, w)``) and the slices are
+    all-gathered into ``gathered [world, rows, out_dim / world]``, so every
+    rank holds ``out = concat(gathered[0], ..., gathered[world-1], dim=1)``
+    while reading only 1/world of W_o."""
+    import torch
+    import torch.distributed as dist
+
+    y = proj_fn(x_full, w_o_slice)
+    if gathered is None:
+        gathered = torch.empty((world, *y.shape), dtype=y.dtype, device=y.device)
+    if y.device.type == "cuda":
+        dist.all_gather_into_tensor(gathered, y.contiguous(), group=group)
+    else:
+        dist.all_gather(list(gathered.unbind(0)), y.contiguous(), group=group)
+    return gathered
+
+
+def assemble_columns(gathered):
+    """[world, rows, cols] slices -> [rows, world * cols] (for checking)."""
+    return gathered.permute(1, 0, 2).reshape(gathered.shape[1], -1)

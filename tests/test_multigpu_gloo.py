@@ -139,3 +139,65 @@ def test_split_k_ranges_cover_each_sequence(pkg):
             blocks += count
         np.testing.assert_array_equal(tot, lens)
         np.testing.assert_array_equal(blocks, (lens + 63) // 64)
+
+
+def _wo_worker(rank, world, port, out_path):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        mg = importlib.import_module(PACKAGE + ".multigpu")
+        rng = np.random.default_rng(7)
+        K, N = 48, 40
+        w_full = torch.as_tensor(rng.standard_normal((K, N)))
+        c0, c1 = mg.column_range(N, world, rank)
+        w_slice = w_full[:, c0:c1].contiguous()
+        proj = lambda x, w: x @ w
+        # split-K: every rank holds the same merged rows
+        x_all = torch.as_tensor(rng.standard_normal((5, K)))
+        out_k = mg.assemble_columns(mg.sharded_out_proj(x_all, w_slice, world, proj))
+        err_k = float((out_k - x_all @ w_full).abs().max())
+        # sequence sharding: rank r holds rows of its own sequences (uneven counts)
+        owner = np.array([0, 1, 1, 0, 1, 1, 1])
+        rows = torch.as_tensor(rng.standard_normal((owner.size, K)))
+        mine = rows[torch.as_tensor(np.nonzero(owner == rank)[0])]
+        max_rows = int(np.bincount(owner, minlength=world).max())
+        g = mg.gather_rows(mine, world, max_rows)
+        out_s = mg.assemble_columns(mg.sharded_out_proj(g.reshape(-1, K), w_slice, world, proj))
+        err_s = 0.0
+        for r in range(world):
+            idx = np.nonzero(owner == r)[0]
+            got = out_s.reshape(world, max_rows, N)[r, :idx.size]
+            err_s = max(err_s, float((got - rows[idx] @ w_full).abs().max()))
+        if rank == 0:
+            with open(out_path, "w") as f:
+                json.dump({"err_k": err_k, "err_s": err_s, "cols": [c0, c1]}, f)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_wo_column_sharding_over_gloo(tmp_path):
+    out = tmp_path / "wo.json"
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_wo_worker, args=(r, 2, port, str(out))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        assert p.exitcode == 0
+    res = json.loads(out.read_text())
+    assert res["err_k"] <= 1e-12 and res["err_s"] <= 1e-12
+    assert res["cols"] == [0, 20]
+
+
+def test_column_range_rejects_uneven(pkg):
+    mg = importlib.import_module(PACKAGE + ".multigpu")
+    assert mg.column_range(7168, 8, 3) == (2688, 3584)
+    with pytest.raises(ValueError):
+        mg.column_range(7168, 3, 0)
