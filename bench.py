@@ -78,6 +78,9 @@ def parse_args():
     ap.add_argument("--path", default="latent", choices=["latent", "fullkv", "materialised"],
                     help="latent: the direct latent decode; fullkv: stored FP16 K/V; "
                          "materialised: K/V rebuilt from the latent pool every step")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="split-K result exchange: peer memory over NVLink (two kernels) or "
+                         "NCCL all-gathers and a merge kernel")
     ap.add_argument("--seqs", type=int, default=0,
                     help="keep only the first N sequences (small profiling cases)")
     return ap.parse_args()
@@ -432,10 +435,14 @@ def run_ours(args, s, rank: int, world: int):
                                                     s.latent_dim, s.value_dim),
                          dtype=torch.uint8, device=dev)
         want_lse = split_k
+        peer_x = (mg.PeerExchange(nb_local * s.q_heads, D, world, rank, dev)
+                  if split_k and args.exchange == "peer" else None)
+        merged = (torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
+                  if peer_x is not None else None)
         gathered_ctx = torch.empty((world, nb_local, s.q_heads, D), dtype=torch.float32,
-                                   device=dev) if split_k else None
+                                   device=dev) if split_k and peer_x is None else None
         gathered_lse = torch.empty((world, nb_local, s.q_heads), dtype=torch.float32,
-                                   device=dev) if split_k else None
+                                   device=dev) if split_k and peer_x is None else None
         K_o = s.q_heads * D
         if wo_sharded:
             # rows projected on every rank: the merged contexts (split-K) or
@@ -482,7 +489,10 @@ def run_ours(args, s, rank: int, world: int):
                                   want_lse=want_lse, workspace=ws, allow_empty=split_k,
                                   phase="combine")
             res = ctx
-            if split_k:
+            if split_k and peer_x is not None:
+                peer_x.publish(ctx, r["lse"])
+                res = peer_x.merge(merged)
+            elif split_k:
                 res = mg.gather_and_merge(ctx, r["lse"], world,
                                           lambda c, l: ops.lse_merge(c, l)[0],
                                           gathered_ctx, gathered_lse)
@@ -501,8 +511,10 @@ def run_ours(args, s, rank: int, world: int):
             return step(q_buf, rows_buf, ev)
 
         # append, partial pass (+ FP16 query staging in tensor-core mode),
-        # combine, query projection, shard merge, W_o GEMM + split reduction
-        launches_per_step = (3 + (mode == "tc") + (0 if s.absorbed else 1) + (1 if split_k else 0)
+        # combine, query projection, shard merge (peer exchange: publish +
+        # merge), W_o GEMM + split reduction
+        launches_per_step = (3 + (mode == "tc") + (0 if s.absorbed else 1)
+                             + ((2 if peer_x is not None else 1) if split_k else 0)
                              + (2 if w_o is not None else 0))
 
     def barrier():
@@ -631,6 +643,8 @@ def run_ours(args, s, rank: int, world: int):
         torch.cuda.synchronize(dev)
         graph.reset()
         graph = None
+    if not args.grow and args.path == "latent" and peer_x is not None:
+        peer_x.close()
     if rank != 0:
         return None
     peaks, peak_kind = load_peaks()
@@ -681,6 +695,7 @@ def run_ours(args, s, rank: int, world: int):
                        "ms_per_step_eager": eager_ms / args.steps,
                        "growing": ("one token per sequence allocated on the device each step"
                                    if args.grow else "no: the append rewrites the last token"),
+                       "exchange": (args.exchange if split_k else None),
                        "parallelism": (f"split-k{world}" if split_k else
                                        (f"dp{world}" if world > 1 else "single")),
                        "l2": "inputs larger than L2 (no flush)" if algo > 126e6

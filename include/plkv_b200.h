@@ -118,6 +118,34 @@ int plkv_reconstruct_kv(const void* latent, int32_t latent_is_f16, int64_t num_s
                         int32_t head_dim, int32_t block_size, void* k_out, void* v_out,
                         int32_t out_is_f16, int32_t* err_flags, plkv_stream_t stream);
 
+/* ---- Split-K result exchange through peer memory (one node, NVLink) ----
+ * Replaces the all-gather + plkv_lse_merge of the split-K shards with two
+ * kernels over buffers that every rank maps (cudaIpc).  Rank r allocates
+ * plkv_peer_buffer_bytes(rows, width) with plkv_peer_alloc, the ranks swap the
+ * 64-byte handles (any host channel), and each rank opens the others' with
+ * plkv_peer_open; bufs is then a DEVICE array of the W base pointers (own one
+ * at index rank) and ctrl a zeroed DEVICE array of 4 uint64 of this rank.
+ * Per step: plkv_peer_publish(ctx[rows, width], lse[rows]) after the rank's
+ * combine, then plkv_peer_merge(out[rows, width], lse_out[rows] or NULL),
+ * which waits (bounded: PLKV_FLAG_TIMEOUT, outputs 0) for every rank's
+ * publish of the step and merges them with the LSE rule.  Every rank issues
+ * the same sequence of steps; world <= 32.  Close and free the buffers only
+ * after every rank's last merge completed (a host barrier). */
+typedef struct plkv_ipc_handle {
+    char bytes[64];
+} plkv_ipc_handle;
+size_t plkv_peer_buffer_bytes(int64_t rows, int32_t width);
+int plkv_peer_alloc(size_t bytes, void** ptr, plkv_ipc_handle* handle);
+int plkv_peer_open(const plkv_ipc_handle* handle, void** ptr);
+int plkv_peer_close(void* ptr);
+int plkv_peer_free(void* ptr);
+int plkv_peer_publish(const float* ctx, const float* lse, int64_t rows, int32_t width,
+                      void* const* bufs, int32_t world, int32_t rank, uint64_t* ctrl,
+                      plkv_stream_t stream);
+int plkv_peer_merge(int64_t rows, int32_t width, void* const* bufs, int32_t world, int32_t rank,
+                    uint64_t* ctrl, float* out, float* lse_out, int32_t* err_flags,
+                    plkv_stream_t stream);
+
 /* Device-side allocation of new token positions (replaces the bump allocator
  * PagedBlockTable.allocate_token_positions, block_table.py:26-38, and
  * BlockTable::allocate_tokens, lib.rs:1346-1364, for a batch on the GPU).

@@ -79,6 +79,13 @@ SIGNATURES = {
     "plkv_latent_append_slots_f16": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _I32, _P, _P]),
     "plkv_reconstruct_kv": (ctypes.c_int, [_P, _I32, _I64, _I32, _I32, _P, _I64, _P, _P, _I32,
                                             _I32, _I32, _P, _P, _I32, _P, _P]),
+    "plkv_peer_buffer_bytes": (_SZ, [_I64, _I32]),
+    "plkv_peer_alloc": (ctypes.c_int, [_SZ, _P, _P]),
+    "plkv_peer_open": (ctypes.c_int, [_P, _P]),
+    "plkv_peer_close": (ctypes.c_int, [_P]),
+    "plkv_peer_free": (ctypes.c_int, [_P]),
+    "plkv_peer_publish": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _I32, _I32, _P, _P]),
+    "plkv_peer_merge": (ctypes.c_int, [_I64, _I32, _P, _I32, _I32, _P, _P, _P, _P, _P]),
     "plkv_allocate_slots": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _I64, _P, _I64, _P,
                                             _P]),
     "plkv_kv_append_f16": (ctypes.c_int, [_P, _P, _P, _I64, _P, _P, _P, _I64, _P, _P, _I64, _I32,

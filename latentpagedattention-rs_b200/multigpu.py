@@ -149,3 +149,123 @@ def sharded_out_proj(x_full, w_o_slice, world: int, proj_fn, gathered=None, grou
 def assemble_columns(gathered):
     """[world, rows, cols] slices -> [rows, world * cols] (for checking)."""
     return gathered.permute(1, 0, 2).reshape(gathered.shape[1], -1)
+
+
+# ------------------------------------------ peer-memory split-K exchange
+
+class PeerExchange:
+    """Split-K result exchange through peer memory (``plkv_peer_*``).
+
+    Rank r publishes its (ctx [rows, width], lse [rows]) in a buffer of its
+    own that every rank of the node has mapped; each rank's merge reads the W
+    ranks' rows over NVLink and applies the LSE rule, so every rank ends with
+    the merged rows.  Replaces ``gather_and_merge`` (two all-gathers and a
+    merge kernel) with two kernels and no collective on the data path; the
+    one collective is the handle swap at construction.  Every rank must call
+    ``publish`` and ``merge`` once per step, in the same order, and ``close``
+    only after its last merge (it synchronises the ranks first)."""
+
+    def __init__(self, rows: int, width: int, world: int, rank: int, device, group=None,
+                 _local_ptrs=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self._lib = _lib
+        L = _lib.lib()
+        self.rows, self.width, self.world, self.rank = int(rows), int(width), world, rank
+        self.device = torch.device(device)
+        self.group = group
+        self.opened, self.own = [], None
+        if _local_ptrs is not None:
+            ptrs = list(_local_ptrs)
+        else:
+            nbytes = int(L.plkv_peer_buffer_bytes(self.rows, self.width))
+            own = ctypes.c_void_p()
+            handle = (ctypes.c_char * 64)()
+            _lib.check(L.plkv_peer_alloc(nbytes, ctypes.byref(own), handle), "plkv_peer_alloc")
+            self.own = own.value
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            ptrs = []
+            for s in range(world):
+                if s == rank:
+                    ptrs.append(self.own)
+                    continue
+                h = (ctypes.c_char * 64).from_buffer_copy(handles[s])
+                p = ctypes.c_void_p()
+                _lib.check(L.plkv_peer_open(h, ctypes.byref(p)), "plkv_peer_open")
+                self.opened.append(p.value)
+                ptrs.append(p.value)
+        self.bufs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.ctrl = torch.zeros(4, dtype=torch.int64, device=self.device)
+
+    @classmethod
+    def local_group(cls, world: int, rows: int, width: int, device):
+        """`world` exchanges over plain buffers of one device (a single-process
+        stand-in for the ranks, for tests): publishes must all precede the
+        merges in stream order.  Returns (exchanges, buffers)."""
+        import torch
+
+        from . import _lib
+
+        nbytes = int(_lib.lib().plkv_peer_buffer_bytes(rows, width))
+        bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=device) for _ in range(world)]
+        ptrs = [b.data_ptr() for b in bufs]
+        return [cls(rows, width, world, r, device, _local_ptrs=ptrs) for r in range(world)], bufs
+
+    def _stream(self):
+        import torch
+
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def publish(self, ctx, lse) -> None:
+        import torch
+
+        for n, t in (("ctx", ctx), ("lse", lse)):
+            if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float32
+                    and t.is_contiguous()):
+                raise TypeError(f"{n} must be a contiguous FP32 CUDA tensor")
+        if ctx.numel() != self.rows * self.width or lse.numel() != self.rows:
+            raise ValueError("ctx / lse do not match the exchange's rows x width")
+        L = self._lib.lib()
+        self._lib.check(L.plkv_peer_publish(ctx.data_ptr(), lse.data_ptr(), self.rows, self.width,
+                                            self.bufs.data_ptr(), self.world, self.rank,
+                                            self.ctrl.data_ptr(), self._stream()),
+                        "plkv_peer_publish")
+
+    def merge(self, out, lse_out=None, flags=None):
+        import torch
+
+        if not (isinstance(out, torch.Tensor) and out.is_cuda and out.dtype == torch.float32
+                and out.is_contiguous() and out.numel() == self.rows * self.width):
+            raise TypeError("out must be a contiguous FP32 CUDA tensor of rows x width")
+        L = self._lib.lib()
+        self._lib.check(L.plkv_peer_merge(self.rows, self.width, self.bufs.data_ptr(), self.world,
+                                          self.rank, self.ctrl.data_ptr(), out.data_ptr(),
+                                          None if lse_out is None else lse_out.data_ptr(),
+                                          None if flags is None else flags.data_ptr(),
+                                          self._stream()),
+                        "plkv_peer_merge")
+        return out
+
+    def close(self) -> None:
+        """Synchronise the ranks, then unmap the peers' buffers and free this
+        rank's (no rank may still read it)."""
+        import torch
+        import torch.distributed as dist
+
+        if self.own is None and not self.opened:
+            return
+        torch.cuda.synchronize(self.device)
+        if dist.is_initialized():
+            dist.barrier(group=self.group)
+        L = self._lib.lib()
+        for p in self.opened:
+            L.plkv_peer_close(p)
+        if self.own is not None:
+            L.plkv_peer_free(self.own)
+        self.opened, self.own = [], None
