@@ -11,6 +11,7 @@ namespace plkv {
 constexpr int kCombineRows = 8;   // (sequence, head) rows per CTA
 constexpr int kMaxWidthPerLane = 20;  // width <= 640
 constexpr int kLSlices = 8;       // latent-row slices of the projection
+constexpr int kItemBatch = 4;     // split-K items whose loads are in flight together
 
 // grid = (proj_heads, ceil(batch * group / kCombineRows)), block = 256.
 // Row r of the CTA is (b, h) with h = p * group + (gr % group), b = gr / group.
@@ -51,16 +52,31 @@ combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_
             for (int i = ib + lane; i < ie; i += 32) M = fmaxf(M, ws.part_m[(int64_t)i * Hq + h]);
             M = warp_max(M);
             if (M != -INFINITY) {
-                for (int i = ib; i < ie; ++i) {
-                    const float mi = ws.part_m[(int64_t)i * Hq + h];
-                    if (mi == -INFINITY) continue;
-                    const float wi = expf(mi - M);
-                    S += ws.part_l[(int64_t)i * Hq + h] * wi;
-                    const float* src = ws.part_ctx + ((int64_t)i * Hq + h) * width;
+                // kItemBatch items per round trip: all their loads are issued
+                // before any is used, so the row costs one memory latency per
+                // batch instead of one per item.  Items in the order i = ib..
+                for (int i0 = ib; i0 < ie; i0 += kItemBatch) {
+                    float wq[kItemBatch], v[kItemBatch][kMaxWidthPerLane];
 #pragma unroll
-                    for (int k = 0; k < kMaxWidthPerLane; ++k) {
-                        const int col = lane + 32 * k;
-                        if (k < ncol && col < width) acc[k] = fmaf(src[col], wi, acc[k]);
+                    for (int q = 0; q < kItemBatch; ++q) {
+                        const int i = i0 + q;
+                        const float mi = i < ie ? ws.part_m[(int64_t)i * Hq + h] : -INFINITY;
+                        wq[q] = mi;
+                        const float* src = ws.part_ctx + ((int64_t)i * Hq + h) * width;
+#pragma unroll
+                        for (int k = 0; k < kMaxWidthPerLane; ++k) {
+                            const int col = lane + 32 * k;
+                            v[q][k] = (mi != -INFINITY && k < ncol && col < width) ? src[col] : 0.f;
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < kItemBatch; ++q) {
+                        const int i = i0 + q;
+                        if (wq[q] == -INFINITY) continue;
+                        const float wi = expf(wq[q] - M);
+                        S += ws.part_l[(int64_t)i * Hq + h] * wi;
+#pragma unroll
+                        for (int k = 0; k < kMaxWidthPerLane; ++k) acc[k] = fmaf(v[q][k], wi, acc[k]);
                     }
                 }
             }
