@@ -322,7 +322,10 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
         // S work thus stays queued on the tensor pipe while the softmax of
         // earlier tiles runs.  S never crosses into the next item before that
         // item's Q is loaded, which waits until every issuer's S of the
-        // current item completed (barrier QFree).
+        // current item completed (barrier QFree).  The barriers are polled
+        // with test_wait, which never suspends: a try_wait on a barrier that
+        // is not ready may put the thread to sleep while another one, which
+        // is, waits to be noticed (about 0.3 us per tile, measured).
         if (leader && lane == 0) {
             const int part = warp == 1 ? 0 : warp == 3 ? 1 : warp == 8 ? 2 : 3;
             const bool has_o = part < 2;  // parts 0 and 1 also issue O half `part`
@@ -339,7 +342,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
             while (has_o ? oi < n_items_w : si < n_items_w) {
                 bool did = false;
                 if (si < n_items_w) {
-                    if (!s_q && mbar_try_wait(mb + kBarQFull, si & 1)) {
+                    if (!s_q && mbar_test_wait(mb + kBarQFull, si & 1)) {
                         s_q = true;
                         tc_fence_after();
                     }
@@ -352,9 +355,9 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                             s_q = false;
                             did = true;
                         } else if ((sg < kSBufs ||
-                                    mbar_try_wait(mb + kBarPFull + 8 * ((sg - kSBufs) & 1),
+                                    mbar_test_wait(mb + kBarPFull + 8 * ((sg - kSBufs) & 1),
                                                   ((sg - kSBufs) >> 1) & 1)) &&
-                                   mbar_try_wait(mb + kBarKFull + 8 * (sg & 1), (sg >> 1) & 1)) {
+                                   mbar_test_wait(mb + kBarKFull + 8 * (sg & 1), (sg >> 1) & 1)) {
                             tc_fence_after();
                             const int st = sg & 1, sb = sg % kSBufs;
                             const uint32_t kreg = sbase + kKOff + st * kKStage;
@@ -382,8 +385,8 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                         go = item_geom(items, i_begin + oi, seq_lens, bs, cap, flags, false);
                     oj = 0;
                     did = true;
-                } else if (og < sg && mbar_try_wait(mb + kBarPFull + 8 * (og & 1), (og >> 1) & 1) &&
-                           (oj > 0 || oi == 0 || mbar_try_wait(mb + kBarOFree, (oi - 1) & 1))) {
+                } else if (og < sg && mbar_test_wait(mb + kBarPFull + 8 * (og & 1), (og >> 1) & 1) &&
+                           (oj > 0 || oi == 0 || mbar_test_wait(mb + kBarOFree, (oi - 1) & 1))) {
                     tc_fence_after();
                     const int st = og & 1;
                     const uint32_t vreg = sbase + kVOff + st * kVStage;
