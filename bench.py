@@ -81,6 +81,10 @@ def parse_args():
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="split-K result exchange: peer memory over NVLink (two kernels) or "
                          "NCCL all-gathers and a merge kernel")
+    ap.add_argument("--kernel-suite", action="store_true",
+                    help="time every kernel of the library on one synthetic case each")
+    ap.add_argument("--suite-reps", type=int, default=5,
+                    help="timed calls per kernel in --kernel-suite (after up to 2 warm-up calls)")
     ap.add_argument("--seqs", type=int, default=0,
                     help="keep only the first N sequences (small profiling cases)")
     return ap.parse_args()
@@ -724,6 +728,185 @@ def run_ours(args, s, rank: int, world: int):
     return line
 
 
+
+def run_kernel_suite(args) -> dict:
+    """Every kernel of the library on one synthetic case each, sized so that
+    its inputs exceed the 126 MB L2 where the operation is bandwidth-bound:
+    CUDA-event time per call (mean of 5 after 2 warm-up calls), algorithmic
+    bytes per call (what the operation must read and write at minimum) and
+    the achieved fraction of the measured HBM bandwidth.  Run under ncu
+    (``-k regex:plkv|tc::``) it gives each kernel's DRAM traffic."""
+    import torch
+
+    ops = importlib.import_module(PACKAGE + ".ops")
+    wl = importlib.import_module(PACKAGE + ".workloads")
+    mg = importlib.import_module(PACKAGE + ".multigpu")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(20260710)
+    peaks, peak_kind = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    f32 = dict(dtype=torch.float32, device=dev)
+
+    def randn(*shape, scale=1.0):
+        return torch.randn(shape, generator=g, device=dev) * scale
+
+    def paged(B, n_tok, bs, per_row_elems, rng_seed):
+        """Block tables of B sequences of n_tok tokens drawn from a permuted pool."""
+        nb = (n_tok + bs - 1) // bs
+        perm = np.random.default_rng(rng_seed).permutation(B * nb).astype(np.int32)
+        tables = torch.as_tensor(perm.reshape(B, nb), device=dev)
+        lens_h = np.full(B, n_tok, np.int32)
+        return tables, lens_h, torch.as_tensor(lens_h, device=dev), B * nb
+
+    results = []
+
+    reps = max(1, args.suite_reps)
+
+    def timed(name, kernels, fn, nbytes, note=""):
+        for _ in range(min(2, reps)):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        results.append({"op": name, "kernels": kernels, "us": round(ms * 1e3, 2),
+                        "algorithmic_bytes": int(nbytes), "GB/s": round(gbs, 1),
+                        "frac_of_hbm": round(gbs / hbm, 3), "note": note})
+
+    # FP32 -> FP16 storage conversion
+    x = randn(64 << 20)
+    y = torch.empty(64 << 20, dtype=torch.int16, device=dev)
+    timed("quantize_f16 (64 Mi values)", ["quantize_f16_kernel"],
+          lambda: ops.lib().plkv_quantize_f16(x.data_ptr(), y.data_ptr(), x.numel(), None,
+                                              torch.cuda.current_stream(dev).cuda_stream),
+          x.numel() * 6)
+    del x, y
+    # latent append through the block tables (long-context batch) and by slot
+    L = 576
+    tables, lens_h, lens, P = paged(8, 131072, 64, L, 1)
+    cache = torch.zeros((P, 64, L), dtype=torch.float16, device=dev)
+    rows = randn(8, L)
+    pos = torch.as_tensor(lens_h - 1, device=dev)
+    timed("latent_append (8 rows, block tables)", ["latent_append_kernel"],
+          lambda: ops.latent_append(rows, cache, tables, positions=pos), 8 * L * 6 + 8 * 4,
+          "launch-bound: 8 rows")
+    n_rows = 65536
+    slots = torch.as_tensor(np.random.default_rng(2).permutation(P * 64)[:n_rows].astype(np.int64),
+                            device=dev)
+    rows_many = randn(n_rows, L)
+    timed("latent_append_slots (65536 rows)", ["latent_append_slots_kernel"],
+          lambda: ops.latent_append_slots(rows_many, cache, slots), n_rows * (L * 6 + 8))
+    del rows_many
+    # tensor-core decode of two long sequences: FP16 query staging, partial pass, combine
+    s = wl.spec("long_context")
+    t2 = tables[:2].contiguous()
+    l2 = lens[:2].contiguous()
+    q_lat = randn(2, 128, L)
+    w_uv = randn(128, 512, 128, scale=1 / math.sqrt(512))
+    plan = ops.plan_workers(lens_h[:2], 64, device=dev)
+    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, 2, 128, L, 512), dtype=torch.uint8,
+                     device=dev)
+    ctx = torch.empty((2, 128, 128), **f32)
+    kw = dict(scale=s.scale, value_dim=512, w_v=w_uv, mode="tc", out=ctx, workspace=ws)
+    tok = 2 * 131072
+    timed("latent decode, tensor-core partial pass (2 x 131072 tokens)",
+          ["q_prep_kernel", "latent_partial_tc_kernel"],
+          lambda: ops.latent_decode(q_lat, cache, t2, l2, plan, phase="partial", **kw),
+          tok * L * 2 + 2 * 128 * L * 4 + 2 * 2048 * 4)
+    timed("latent decode, combine + W_uv (2 sequences)", ["combine_project_kernel"],
+          lambda: ops.latent_decode(q_lat, cache, t2, l2, plan, phase="combine", **kw),
+          plan.n_items * 128 * (512 + 2) * 4 + w_uv.numel() * 4 + 2 * 128 * 128 * 4)
+    del cache, ws
+    # exact FP32 decode of GQA shapes (write-then-attend sizes), latent and full-KV
+    B, n_tok, bs, Hq, KV, D, Lg = 64, 4096, 16, 32, 8, 128, 256
+    tables, lens_h, lens, P = paged(B, n_tok, bs, Lg, 3)
+    cache = (randn(P, bs, Lg)).half()
+    qg = randn(B, Hq, D)
+    w_k = randn(KV, Lg, D, scale=1 / math.sqrt(D))
+    w_v = randn(KV, Lg, D, scale=1 / math.sqrt(Lg))
+    qlat_buf = torch.empty((B, Hq, Lg), **f32)
+    timed("project_query (64 x 32 heads, L = 256)", ["project_query_kernel"],
+          lambda: ops.project_query(qg, w_k, out=qlat_buf),
+          qg.numel() * 4 + w_k.numel() * 4 + qlat_buf.numel() * 4)
+    plan = ops.plan_splits(lens_h, bs, device=dev)
+    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, B, Hq, Lg, Lg), dtype=torch.uint8,
+                     device=dev)
+    ctx = torch.empty((B, Hq, D), **f32)
+    kw = dict(scale=1 / math.sqrt(D), value_dim=Lg, w_v=w_v, mode="exact", out=ctx, workspace=ws)
+    timed("latent decode, exact partial pass (64 x 4096 tokens, GQA)", ["latent_partial_exact_kernel"],
+          lambda: ops.latent_decode(qlat_buf, cache, tables, lens, plan, phase="partial", **kw),
+          B * n_tok * Lg * 2 + B * Hq * Lg * 4, "FP32 CUDA-core bound (64 FLOP/byte)")
+    timed("latent decode, exact combine + W_v", ["combine_project_kernel"],
+          lambda: ops.latent_decode(qlat_buf, cache, tables, lens, plan, phase="combine", **kw),
+          plan.n_items * Hq * (Lg + 2) * 4 + w_v.numel() * 4 + ctx.numel() * 4)
+    # materialised reconstruction of every active token's K / V, then the full-KV decode
+    k16 = torch.zeros((P, KV, bs, D), dtype=torch.float16, device=dev)
+    v16 = torch.zeros_like(k16)
+    tab = tables.cpu().numpy()
+    act = torch.as_tensor(np.concatenate([tab[i, np.arange(n_tok) // bs].astype(np.int64) * bs
+                                          + np.arange(n_tok) % bs for i in range(B)]), device=dev)
+    n_act = act.numel()
+    timed("reconstruct_kv (262144 rows, L = 256 -> 8 x 128, FP16 out)", ["reconstruct_kv_kernel"],
+          lambda: ops.reconstruct_kv(cache, w_k, w_v, slots=act, block_size=bs, k_out=k16,
+                                     v_out=v16),
+          n_act * (Lg * 2 + 8 + 2 * KV * D * 2) + (w_k.numel() + w_v.numel()) * 4,
+          "FP32 CUDA-core bound (2 x 256 x 2048 FLOP per row)")
+    fws = torch.empty(int(ops.lib().plkv_fullkv_decode_workspace_size(plan.n_items, B, Hq, D)),
+                      dtype=torch.uint8, device=dev)
+    timed("full-KV decode (64 x 4096 tokens, 8 KV heads, FP16)",
+          ["fullkv_partial_exact_kernel", "combine_project_kernel"],
+          lambda: ops.fullkv_decode(qg, k16, v16, tables, lens, plan, scale=1 / math.sqrt(D),
+                                    out=ctx, workspace=fws),
+          B * n_tok * KV * D * 2 * 2 + qg.numel() * 4 + ctx.numel() * 4)
+    kr, vr = randn(B, KV, D), randn(B, KV, D)
+    posg = torch.as_tensor(lens_h - 1, device=dev)
+    timed("kv_append (64 rows)", ["kv_append_kernel"],
+          lambda: ops.kv_append(kr, vr, k16, v16, tables, positions=posg),
+          B * KV * D * 2 * 6, "launch-bound")
+    del cache, k16, v16, fws, ws
+    # token allocation for 65536 sequences
+    nseq = 65536
+    tab_a = torch.full((nseq, 4), -1, dtype=torch.int32, device=dev)
+    lens_a = torch.zeros(nseq, dtype=torch.int32, device=dev)
+    nb = torch.zeros(1, dtype=torch.int32, device=dev)
+    slots_a = torch.empty(nseq, dtype=torch.int64, device=dev)
+
+    def alloc():
+        lens_a.zero_()
+        ops.allocate_slots(tab_a, lens_a, nb, 1 << 30, 64, slots=slots_a)
+    timed("allocate_slots (65536 sequences, one token each)", ["allocate_slots_kernel"], alloc,
+          nseq * (4 + 4 + 4 + 8), "one CTA: a scan over the batch (includes a 256 KB memset)")
+    # W_o output projection, LSE merge of 8 shards, peer-memory exchange (2 stand-in ranks)
+    w_o = randn(16384, 7168, scale=1 / math.sqrt(16384))
+    xo = randn(64, 16384)
+    oo = torch.empty((64, 7168), **f32)
+    timed("out_proj W_o (64 x 16384 x 7168, FP32)", ["out_proj_partial_kernel", "out_proj_reduce_kernel"],
+          lambda: ops.out_proj(xo, w_o, out=oo), w_o.numel() * 4 + xo.numel() * 4 + oo.numel() * 4,
+          "FP32 CUDA-core bound (15 GFLOP)")
+    del w_o
+    cs, ls = randn(8, 1024, 128), randn(8, 1024)
+    timed("lse_merge (8 shards x 1024 rows x 128)", ["lse_merge_kernel"],
+          lambda: ops.lse_merge(cs, ls), cs.numel() * 4 + ls.numel() * 4 + 1024 * 129 * 4)
+    exch, _bufs = mg.PeerExchange.local_group(2, 1024, 128, dev)
+    mo = torch.empty((1024, 128), **f32)
+
+    def peer_step():
+        exch[0].publish(cs[0].contiguous(), ls[0].contiguous())
+        exch[1].publish(cs[1].contiguous(), ls[1].contiguous())
+        exch[0].merge(mo)
+        exch[1].merge(mo)
+    timed("peer exchange: 2 publishes + 2 merges (1024 rows x 128)",
+          ["publish_kernel", "merge_kernel"], peer_step, 2 * (1024 * 129 * 4) * 3,
+          "one GPU standing in for two ranks")
+    return {"kernel_suite": results, "peak_GB/s": hbm, "peak_source": f"{peak_kind} hbm_gbs"}
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -736,6 +919,9 @@ def main():
         s = dataclasses.replace(s, batch=args.seqs, lens=s.lens[:args.seqs])
     if args.impl == "reference":
         run_reference(args, s, rank, world)
+        return
+    if args.kernel_suite:
+        print(json.dumps(run_kernel_suite(args)), flush=True)
         return
     import torch
     import torch.distributed as dist

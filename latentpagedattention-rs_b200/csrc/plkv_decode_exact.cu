@@ -405,23 +405,32 @@ project_query_kernel(const float* __restrict__ q, const float* __restrict__ w_k,
     for (int i = tid; i < G * D; i += 256) qs[i] = q[((int64_t)b * Hq + g * G) * D + i];
     __syncthreads();
     constexpr int kMaxPerLane = 8;  // D <= 256
-    for (int l = warp; l < L; l += 8) {
-        const float* wr = w_k + ((int64_t)g * L + l) * D;
-        float wv[kMaxPerLane];
+    constexpr int kRows = 4;        // latent rows per warp iteration, loads in flight together
+    for (int l0 = warp; l0 < L; l0 += 8 * kRows) {
+        float wv[kRows][kMaxPerLane];
 #pragma unroll
-        for (int i = 0; i < kMaxPerLane; ++i) {
-            int d = lane + 32 * i;
-            wv[i] = d < D ? wr[d] : 0.f;
-        }
-        for (int j = 0; j < G; ++j) {
-            float acc = 0.f;
+        for (int r = 0; r < kRows; ++r) {
+            const int l = l0 + 8 * r;
+            const float* wr = w_k + ((int64_t)g * L + l) * D;
 #pragma unroll
             for (int i = 0; i < kMaxPerLane; ++i) {
-                int d = lane + 32 * i;
-                if (d < D) acc = fmaf(wv[i], qs[j * D + d], acc);
+                const int d = lane + 32 * i;
+                wv[r][i] = (l < L && d < D) ? wr[d] : 0.f;
             }
-            acc = warp_sum(acc);
-            if (lane == 0) q_lat[((int64_t)b * Hq + g * G + j) * L + l] = acc;
+        }
+        for (int j = 0; j < G; ++j) {
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < kMaxPerLane; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < D) acc = fmaf(wv[r][i], qs[j * D + d], acc);
+                }
+                acc = warp_sum(acc);
+                const int l = l0 + 8 * r;
+                if (lane == 0 && l < L) q_lat[((int64_t)b * Hq + g * G + j) * L + l] = acc;
+            }
         }
     }
 }

@@ -78,7 +78,10 @@ publish_kernel(const float* __restrict__ ctx, const float* __restrict__ lse, int
         dst[i] = ctx[i];
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows; i += stride)
         dst[n_ctx + i] = lse[i];
-    __threadfence_system();
+    // Device scope here: the last CTA observes every CTA's writes through the
+    // counter below, and its system-scope release of the flags (cumulative)
+    // then publishes them to the peers.
+    __threadfence();
     __syncthreads();
     __shared__ bool last;
     if (threadIdx.x == 0) {
@@ -133,15 +136,23 @@ merge_kernel(int64_t rows, int width, void* const* __restrict__ bufs, int world,
         for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
         const float inv = (ok_s && den > 0.f) ? 1.f / den : 0.f;
         // Every lane runs the same iterations (the shuffles name the whole
-        // warp); only the loads and stores are guarded by the width.
+        // warp); only the loads and stores are guarded by the width.  The
+        // sources' values of a column are all loaded before any is used, so
+        // the remote reads of one row are in flight together.
+        float wsrc[kMaxPeers];
+#pragma unroll
+        for (int s = 0; s < kMaxPeers; ++s) wsrc[s] = __shfl_sync(0xffffffffu, w, s);
         for (int c0 = 0; c0 < width; c0 += 32) {
             const int c = c0 + lane;
+            float v[kMaxPeers];
+#pragma unroll
+            for (int s = 0; s < kMaxPeers; ++s)
+                v[s] = (s < world && wsrc[s] != 0.f && c < width)
+                           ? slot(bufs[s], parity, rows, width)[row * width + c]
+                           : 0.f;
             float acc = 0.f;
-            for (int s = 0; s < world; ++s) {
-                const float ws = __shfl_sync(0xffffffffu, w, s);
-                if (ws != 0.f && c < width)
-                    acc = fmaf(ws, slot(bufs[s], parity, rows, width)[row * width + c], acc);
-            }
+#pragma unroll
+            for (int s = 0; s < kMaxPeers; ++s) acc = fmaf(wsrc[s], v[s], acc);
             if (c < width) out[row * width + c] = acc * inv;
         }
         if (lse_out && lane == 0) lse_out[row] = den > 0.f ? M + logf(den) : -INFINITY;
@@ -205,7 +216,7 @@ int plkv_peer_publish(const float* ctx, const float* lse, int64_t rows, int32_t 
         world > plkv::kMaxPeers || (reinterpret_cast<uintptr_t>(ctx) & 15))
         return PLKV_ERR_INVALID_ARGUMENT;
     const int64_t work = rows * width / 4 + rows;
-    const int grid = (int)std::min<int64_t>((work + 255) / 256, 148);
+    const int grid = (int)std::min<int64_t>((work + 255) / 256, 32);
     plkv::publish_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(ctx, lse, rows, width, bufs,
                                                                   world, rank, ctrl);
     return cudaGetLastError() == cudaSuccess ? PLKV_OK : PLKV_ERR_CUDA;
