@@ -199,11 +199,14 @@ int plkv_plan_splits(const int32_t* seq_lens_host, int32_t batch, int32_t block_
                      int32_t max_items, int32_t* seq_item_begin_host, int32_t* n_items_host);
 
 /* Host-side balanced planner for the persistent tensor-core decode: the
- * blocks of all sequences, in sequence order, are cut into `n_workers`
- * contiguous ranges of equal size (+-1 block); every (worker, sequence)
- * overlap becomes one item.  Worker w processes items
- * worker_item_begin_host[w] .. [w+1] in order; items are ordered by sequence
- * as for plkv_plan_splits (seq_item_begin_host has batch + 1 entries) and a
+ * blocks of all sequences, in sequence order, are cut into at most
+ * `n_workers` contiguous ranges; every (worker, sequence) overlap becomes one
+ * item.  A worker's cost is its blocks plus max(1, ceil(256 / block_size))
+ * per item (an item reloads the query, refills the pipeline and writes its
+ * partial context), and the ranges minimise the largest cost.  Worker w
+ * processes items worker_item_begin_host[w] .. [w+1] in order (trailing
+ * workers may get none); items are ordered by sequence as for
+ * plkv_plan_splits (seq_item_begin_host has batch + 1 entries) and a
  * sequence of length 0 still gets one empty item.  Same return codes. */
 int plkv_plan_workers(const int32_t* seq_lens_host, int32_t batch, int32_t block_size,
                       int32_t n_workers, plkv_work_item* items_host, int32_t max_items,

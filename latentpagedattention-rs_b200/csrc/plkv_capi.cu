@@ -175,38 +175,67 @@ int plkv_plan_workers(const int32_t* seq_lens_host, int32_t batch, int32_t block
                       int32_t* n_items_host) {
     if (batch <= 0 || block_size <= 0 || n_workers <= 0) return PLKV_ERR_ZERO_VALUE;
     if (!seq_lens_host || !n_items_host) return PLKV_ERR_INVALID_ARGUMENT;
-    std::vector<int64_t> nb(batch), start(batch + 1, 0);
+    std::vector<int64_t> nb(batch);
+    int64_t total = 0;
     for (int b = 0; b < batch; ++b) {
         if (seq_lens_host[b] < 0) return PLKV_ERR_INVALID_ARGUMENT;
         nb[b] = (seq_lens_host[b] + block_size - 1) / block_size;
-        start[b + 1] = start[b] + nb[b];
+        total += nb[b];
     }
-    const int64_t total = start[batch];
-    // Worker w owns global blocks [bound(w), bound(w+1)).
-    auto bound = [&](int64_t w) { return total * w / n_workers; };
+    // Cost of a worker = its blocks + kItemCost per item: every item reloads
+    // the query, refills the pipeline and writes its partial context (about
+    // four 64-token tiles of time on B200).  Sequences are walked in order and
+    // each worker is filled up to a makespan T; the smallest T that needs at
+    // most n_workers workers is found by bisection (the fill is monotone in T).
+    const int64_t item_cost = std::max<int64_t>(1, (256 + block_size - 1) / block_size);
     std::vector<plkv_work_item> items;
     std::vector<int32_t> item_worker;
     std::vector<int32_t> seq_begin(batch + 1, 0);
-    int64_t w = 0;
-    for (int b = 0; b < batch; ++b) {
-        seq_begin[b] = (int32_t)items.size();
-        if (nb[b] == 0) {
-            // Empty sequence: one empty item, on the worker owning this position.
-            while (w + 1 < n_workers && bound(w + 1) <= start[b]) ++w;
-            items.push_back({b, 0, 0, 0});
-            item_worker.push_back((int32_t)w);
-            continue;
+    auto fill = [&](int64_t T, bool emit) -> int64_t {  // workers used, or n_workers + 1
+        int64_t w = 0, used = 0;
+        for (int b = 0; b < batch; ++b) {
+            if (emit) seq_begin[b] = (int32_t)items.size();
+            if (nb[b] == 0) {  // an empty sequence still gets one (empty) item
+                if (used > 0 && used + item_cost > T) {
+                    ++w;
+                    used = 0;
+                }
+                if (w >= n_workers) return n_workers + 1;
+                used += item_cost;
+                if (emit) {
+                    items.push_back({b, 0, 0, 0});
+                    item_worker.push_back((int32_t)w);
+                }
+                continue;
+            }
+            int64_t pos = 0;
+            while (pos < nb[b]) {
+                if (used > 0 && used + item_cost >= T) {
+                    ++w;
+                    used = 0;
+                }
+                if (w >= n_workers) return n_workers + 1;
+                const int64_t take = std::min(nb[b] - pos, std::max<int64_t>(1, T - used - item_cost));
+                if (emit) {
+                    items.push_back({b, (int32_t)pos, (int32_t)(pos + take), 0});
+                    item_worker.push_back((int32_t)w);
+                }
+                used += item_cost + take;
+                pos += take;
+            }
         }
-        int64_t pos = start[b];
-        while (pos < start[b + 1]) {
-            while (bound(w + 1) <= pos) ++w;
-            const int64_t end = std::min(start[b + 1], bound(w + 1));
-            items.push_back({b, (int32_t)(pos - start[b]), (int32_t)(end - start[b]), 0});
-            item_worker.push_back((int32_t)w);
-            pos = end;
-        }
+        if (emit) seq_begin[batch] = (int32_t)items.size();
+        return w + 1;
+    };
+    int64_t lo = item_cost + 1, hi = total + item_cost * (int64_t)batch + 1;
+    while (lo < hi) {
+        const int64_t mid = lo + (hi - lo) / 2;
+        if (fill(mid, false) <= n_workers)
+            hi = mid;
+        else
+            lo = mid + 1;
     }
-    seq_begin[batch] = (int32_t)items.size();
+    fill(lo, true);
     *n_items_host = (int32_t)items.size();
     if ((int64_t)items.size() > max_items || !items_host || !seq_item_begin_host ||
         !worker_item_begin_host)

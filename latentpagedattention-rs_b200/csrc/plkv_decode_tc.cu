@@ -25,8 +25,11 @@
 // offsets in both CTAs, so each CTA loads its own token half of all nine
 // 64-column blocks into the K ring (consumed by S, released when S is done)
 // and both token halves of its four value blocks into the V ring (consumed by
-// O): 17 TMA boxes of 32 rows x 64 columns per tile and CTA.  Decoupling the
-// rings lets the next tiles' K loads start as soon as S completes.
+// O): per tile and CTA one 3-D TMA copy of 36 KiB (K) and two 4-D copies of
+// 16 KiB (V).  Small 2-D boxes (32 rows x 64 columns, 17 per tile) cost TMA
+// issue time: from L2, nine such boxes per 36 KiB stream at 59 GB/s per SM
+// and one 3-D box at 104 GB/s (measured on B200).  Decoupling the rings lets
+// the next tiles' K loads start as soon as S completes.
 //
 // The query is converted once per call (q_prep kernel) to FP16 pre-scaled by
 // scale * log2(e) and loaded per item by TMA.  Softmax runs in the log2
@@ -122,13 +125,30 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-// Plain (one-CTA) tile load that completes on a barrier of this CTA.
-__device__ __forceinline__ void tma_load_2d_own(uint32_t dst, const CUtensorMap* map, int x, int y,
+// Rows [y, y + box rows) x all nine 64-column blocks in one instruction: the
+// 3-D view (64 columns, rows, 9 column blocks at 128 B) of a row-major FP16
+// matrix of 576 columns lands block after block, each block 128 B per row,
+// which is the K-major SWIZZLE_128B operand layout of the MMAs.  Completes on
+// a barrier of the leader CTA (cta_group::2); no multicast.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int y,
+                                                 uint32_t cluster_bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(0), "r"(cluster_bar),
+          "l"(policy)
+        : "memory");
+}
+// The four value column blocks {z0, z0+1, z0+4, z0+5} of 32 rows in one
+// instruction: 4-D view (64 columns, rows, 4 blocks at 128 B, 2 groups of
+// blocks at 512 B); completes on a barrier of this CTA.
+__device__ __forceinline__ void tma_load_4d_own(uint32_t dst, const CUtensorMap* map, int y, int z0,
                                                 uint32_t bar, uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z0), "r"(0), "r"(bar),
+          "l"(policy)
         : "memory");
 }
 
@@ -170,7 +190,8 @@ __device__ __forceinline__ int half_row(const ItemGeom& g, int j, int h,
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
-latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
+latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
+                         const __grid_constant__ CUtensorMap v_map,
                          const __grid_constant__ CUtensorMap q_map,
                          const uint16_t* __restrict__ cache, int bs,
                          const int32_t* __restrict__ tables, int64_t max_blocks,
@@ -220,7 +241,8 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
         tmem_relinquish_pair();
     }
     if (warp == 0 && lane == 0) {
-        prefetch_tensormap(&cache_map);
+        prefetch_tensormap(&k_map);
+        prefetch_tensormap(&v_map);
         prefetch_tensormap(&q_map);
     }
     tc_fence_before();
@@ -246,8 +268,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                         return false;
                     if (leader) mbar_arrive_expect_tx(mb + kBarQFull, kQTx);
                     const int y = g.seq * kHeads + kHeadsPerCta * (int)rank;
-                    for (int c = 0; c < kKBlocks; ++c)
-                        tma_load_2d_pair(sbase + kQOff + c * kQAtom, &q_map, c * 64, y, qfull, pol);
+                    tma_load_3d_pair(sbase + kQOff, &q_map, y, qfull, pol);
                     return true;
                 };
                 // The first K tiles of an item only need free K stages; Q waits
@@ -277,8 +298,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                     if (leader) mbar_arrive_expect_tx(mb + kBarKFull + 8 * st, kKTx);
                     const uint32_t dst = sbase + kKOff + st * kKStage;
                     const uint32_t fb = st ? kfull1 : kfull0;
-                    for (int c = 0; c < kKBlocks; ++c)
-                        tma_load_2d_pair(dst + c * kBox, &cache_map, c * 64, y, fb, pol);
+                    tma_load_3d_pair(dst, &k_map, y, fb, pol);
                 }
                 if (ok && pre == g.n_tiles) ok = load_q();
                 gt += g.n_tiles;
@@ -303,11 +323,8 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                     mbar_arrive_expect_tx(mb + kBarVFull + 8 * st, kVTx);
                     const uint32_t dst = sbase + kVOff + st * kVStage;
                     for (int h = 0; h < 2; ++h)
-                        for (int s = 0; s < 4; ++s) {
-                            const int cb = (s >> 1) * 4 + (s & 1) + 2 * (int)rank;
-                            tma_load_2d_own(dst + h * 4 * kBox + s * kBox, &cache_map, cb * 64,
-                                            h ? y1 : y0, mb + kBarVFull + 8 * st, pol);
-                        }
+                        tma_load_4d_own(dst + h * 4 * kBox, &v_map, h ? y1 : y0, 2 * (int)rank,
+                                        mb + kBarVFull + 8 * st, pol);
                 }
                 gt += g.n_tiles;
             }
@@ -575,9 +592,16 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
                 ws.part_m[row] = (ok && m_use != -INFINITY) ? m_use * kLn2 : -INFINITY;
                 ws.part_l[row] = ok ? l_tot : 0.f;
             }
-            float* dst = ws.part_ctx + row * kValue;
+            // Context rows, staged through the two P buffers (idle: every O
+            // MMA of the item completed) so that the global stores are whole
+            // 128-byte lines: thread t holds 32 columns of one head, and a
+            // warp stores four heads' 128-byte segments per instruction.
+            // Storing straight from the TMEM lanes (one head per thread, a
+            // 2 KiB stride between threads) took 5.3 us per item.
             const bool have = ok && g.n_tiles > 0;
             if (have) tc_fence_after();
+            uint8_t* stage = smem + kPOff;  // [128 threads][8 chunks of 16 B], chunk c at c ^ (t & 7)
+            float* ctx_base = ws.part_ctx + ((int64_t)ii * kHeads + kHeadsPerCta * rank) * kValue;
 #pragma unroll 1
             for (int u = 0; u < 8; ++u) {
                 float o[32];
@@ -588,11 +612,20 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap cache_map,
 #pragma unroll
                     for (int e = 0; e < 32; ++e) o[e] = 0.f;
                 }
-                const int col = (u >> 2) * 256 + th * 128 + (u & 3) * 32;
+                named_sync_softmax();  // the previous iteration's reads of the stage are done
 #pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                    *reinterpret_cast<float4*>(dst + col + e) =
-                        make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<float4*>(stage + t * 128 + ((c ^ (t & 7)) << 4)) =
+                        make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                named_sync_softmax();
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int idx = t + 128 * k, r = idx >> 3, c = idx & 7;
+                    const float4 v =
+                        *reinterpret_cast<const float4*>(stage + r * 128 + ((c ^ (r & 7)) << 4));
+                    const int col = (u >> 2) * 256 + (r >> 6) * 128 + (u & 3) * 32 + 4 * c;
+                    *reinterpret_cast<float4*>(ctx_base + (int64_t)(r & 63) * kValue + col) = v;
+                }
             }
             tc_fence_before();
             named_sync_softmax();
@@ -641,15 +674,12 @@ static bool load_encode() {
     return g_encode != nullptr;
 }
 
-static bool encode_2d_f16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
-                          uint32_t box_cols, uint32_t box_rows) {
-    cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols * 2};
-    cuuint32_t box[2] = {box_cols, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
-                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+static bool encode_f16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                       const cuuint64_t* strides, const cuuint32_t* box) {
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base),
+                    dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -667,11 +697,18 @@ bool tc_supported(const plkv_latent_decode_args& a) {
 cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWorkspace ws,
                                      cudaStream_t st) {
     if (!tc::load_encode() || !ws.q16) return cudaErrorNotSupported;
-    CUtensorMap cache_map, q_map;
-    if (!tc::encode_2d_f16(&cache_map, a.cache, tc::kLatent,
-                           static_cast<uint64_t>(a.num_physical) * a.block_size, 64, 32) ||
-        !tc::encode_2d_f16(&q_map, ws.q16, tc::kLatent, static_cast<uint64_t>(a.batch) * tc::kHeads,
-                           64, 64))
+    CUtensorMap k_map, v_map, q_map;
+    const cuuint64_t rows = static_cast<uint64_t>(a.num_physical) * a.block_size;
+    const cuuint64_t row_bytes = tc::kLatent * 2;
+    const cuuint64_t k_dims[3] = {64, rows, tc::kKBlocks}, k_str[2] = {row_bytes, 128};
+    const cuuint32_t k_box[3] = {64, 32, tc::kKBlocks};
+    const cuuint64_t v_dims[4] = {64, rows, 4, 2}, v_str[3] = {row_bytes, 128, 512};
+    const cuuint32_t v_box[4] = {64, 32, 2, 2};
+    const cuuint64_t q_dims[3] = {64, static_cast<uint64_t>(a.batch) * tc::kHeads, tc::kKBlocks};
+    const cuuint32_t q_box[3] = {64, tc::kHeadsPerCta, tc::kKBlocks};
+    if (!tc::encode_f16(&k_map, a.cache, 3, k_dims, k_str, k_box) ||
+        !tc::encode_f16(&v_map, a.cache, 4, v_dims, v_str, v_box) ||
+        !tc::encode_f16(&q_map, ws.q16, 3, q_dims, k_str, q_box))
         return cudaErrorInvalidValue;
     const int64_t n4 = (int64_t)a.batch * tc::kHeads * tc::kLatent / 4;
     int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
@@ -690,7 +727,7 @@ cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWor
     }
     const int workers = (a.worker_item_begin && a.n_workers > 0) ? a.n_workers : a.n_items;
     tc::latent_partial_tc_kernel<<<2 * workers, 320, tc::kSmemBytes, st>>>(
-        cache_map, q_map, a.cache, a.block_size, a.block_tables, a.max_blocks, a.num_physical,
+        k_map, v_map, q_map, a.cache, a.block_size, a.block_tables, a.max_blocks, a.num_physical,
         a.seq_lens,
         a.items, (a.worker_item_begin && a.n_workers > 0) ? a.worker_item_begin : nullptr, ws,
         flags);

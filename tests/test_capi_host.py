@@ -185,4 +185,17 @@ def test_worker_plan_balances_and_covers(lens, bs, workers):
     per_worker = [int(np.sum(items[wbegin[w]:wbegin[w + 1], 2] - items[wbegin[w]:wbegin[w + 1], 1]))
                   for w in range(workers)]
     assert sum(per_worker) == total
-    assert max(per_worker) - min(per_worker) <= 1
+    # worker cost = blocks + per-item cost; the plan is never worse than an
+    # equal split of the blocks (whose workers may hold two items)
+    c = max(1, (256 + bs - 1) // bs)
+    cost = [per_worker[w] + c * int(wbegin[w + 1] - wbegin[w]) for w in range(workers)]
+    nb = np.array([(n + bs - 1) // bs for n in lens])
+    start = np.concatenate([[0], np.cumsum(nb)])
+    eq = []
+    for w in range(workers):
+        a, b = total * w // workers, total * (w + 1) // workers
+        n_it = sum(1 for s in range(len(lens)) if (nb[s] == 0 and a <= start[s] < max(b, a + 1))
+                   or (min(b, start[s + 1]) > max(a, start[s])))
+        eq.append((b - a) + c * n_it)
+    assert max(cost) <= max(eq)
+    assert max(cost) <= -(-(total + c * len(lens)) // workers) + 2 * c
