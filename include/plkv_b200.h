@@ -251,7 +251,7 @@ typedef struct plkv_latent_decode_args {
     float* probs;                 /* optional [batch, q_heads, max_seq_len]; masked = 0 */
     int32_t max_seq_len;
     int32_t mode;                 /* PLKV_MODE_* */
-    void* workspace;
+    void* workspace;              /* device memory, 256-byte aligned */
     size_t workspace_bytes;
     int32_t* err_flags;           /* optional */
 } plkv_latent_decode_args;
@@ -335,7 +335,7 @@ typedef struct plkv_fullkv_decode_args {
     float* scores;
     float* probs;
     int32_t max_seq_len;
-    void* workspace;
+    void* workspace;              /* device memory, 256-byte aligned */
     size_t workspace_bytes;
     int32_t* err_flags;
 } plkv_fullkv_decode_args;

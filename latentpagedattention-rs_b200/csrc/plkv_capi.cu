@@ -293,6 +293,7 @@ static int validate_latent(const plkv_latent_decode_args* a) {
     if (a->workspace_bytes <
         decode_workspace_bytes(a->n_items, a->batch, a->q_heads, a->latent_dim, a->value_dim))
         return PLKV_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(a->workspace) & 255) return PLKV_ERR_INVALID_ARGUMENT;
     if (a->n_workers < 0 || (a->n_workers > 0 && !a->worker_item_begin))
         return PLKV_ERR_INVALID_ARGUMENT;
     if (a->mode != PLKV_MODE_EXACT_F32 && a->mode != PLKV_MODE_TC_F16) return PLKV_ERR_UNSUPPORTED;
@@ -388,6 +389,7 @@ int plkv_fullkv_decode(const plkv_fullkv_decode_args* a, plkv_stream_t stream) {
     if (a->workspace_bytes <
         decode_workspace_bytes(a->n_items, a->batch, a->q_heads, 0, a->head_dim))
         return PLKV_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(a->workspace) & 255) return PLKV_ERR_INVALID_ARGUMENT;
     DecodeWorkspace ws = carve_workspace(a->workspace, a->n_items, a->batch, a->q_heads, 0,
                                          a->head_dim);
     cudaStream_t s = (cudaStream_t)stream;

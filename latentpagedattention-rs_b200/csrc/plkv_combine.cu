@@ -13,15 +13,32 @@ constexpr int kMaxWidthPerLane = 20;  // width <= 640
 constexpr int kLSlices = 8;       // latent-row slices of the projection
 constexpr int kItemBatch = 4;     // split-K items whose loads are in flight together
 
+// W is read by every step: its lines are kept in L2 (evict_last) while the
+// partial pass streams the cache through L2 with evict_first.
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ float4 ldg_f4_keep(const float4* ptr, uint64_t pol) {
+    float4 v;
+    asm("ld.global.nc.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+        : "l"(ptr), "l"(pol));
+    return v;
+}
+
 // grid = (proj_heads, ceil(batch * group / kCombineRows)), block = 256.
 // Row r of the CTA is (b, h) with h = p * group + (gr % group), b = gr / group.
 // Phase 1: warp per row merges the row's items in registers (lane owns
 //   columns lane + 32k):  M = max_i m_i,  S = sum_i l_i exp(m_i - M),
 //   c[col] = sum_i ctx_i[col] exp(m_i - M) / S.
 // Phase 2: out[d] = sum_l c[l] * W[p, l, d] (lib.rs:1066-1071).  With
-//   d % 4 == 0 and D <= 128 the 256 threads are (latent slice s) x (group of
-//   4 columns): each thread sums its slice of l with float4 weight loads, then
-//   the slices are added in a fixed order; otherwise a column per thread.
+//   d % 4 == 0, D <= 128 and W 16-byte aligned the 256 threads are (latent
+//   slice s) x (group of 4 columns): each thread sums its slice of l with
+//   float4 weight loads, then the slices are added in a fixed order; otherwise
+//   a column per thread.  W[p] (width x D floats) is prefetched into L2 when
+//   the CTA starts, so that its loads overlap phase 1 instead of following it.
 // Without a projection, c itself is written.
 __global__ void __launch_bounds__(256)
 combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_begin, int B,
@@ -37,6 +54,12 @@ combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_
     const int r0 = blockIdx.y * kCombineRows;
     const int nrows = min(kCombineRows, rows_total - r0);
     const int ncol = (width + 31) / 32;
+    const bool vec_w = w && (D & 3) == 0 && D <= 128 &&
+                       (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+    if (vec_w && tid == 0) {
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                     ::"l"(w + (int64_t)p * width * D), "r"((uint32_t)(width * D * 4)) : "memory");
+    }
 
     for (int r = warp; r < kCombineRows; r += 8) {
         float acc[kMaxWidthPerLane];
@@ -56,25 +79,26 @@ combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_
                 // before any is used, so the row costs one memory latency per
                 // batch instead of one per item.  Items in the order i = ib..
                 for (int i0 = ib; i0 < ie; i0 += kItemBatch) {
-                    float wq[kItemBatch], v[kItemBatch][kMaxWidthPerLane];
+                    // The context loads do not wait for the item's max: an
+                    // item without tokens is skipped below, whatever its row.
+                    float wq[kItemBatch], lq[kItemBatch], v[kItemBatch][kMaxWidthPerLane];
 #pragma unroll
                     for (int q = 0; q < kItemBatch; ++q) {
                         const int i = i0 + q;
-                        const float mi = i < ie ? ws.part_m[(int64_t)i * Hq + h] : -INFINITY;
-                        wq[q] = mi;
+                        wq[q] = i < ie ? ws.part_m[(int64_t)i * Hq + h] : -INFINITY;
+                        lq[q] = i < ie ? ws.part_l[(int64_t)i * Hq + h] : 0.f;
                         const float* src = ws.part_ctx + ((int64_t)i * Hq + h) * width;
 #pragma unroll
                         for (int k = 0; k < kMaxWidthPerLane; ++k) {
                             const int col = lane + 32 * k;
-                            v[q][k] = (mi != -INFINITY && k < ncol && col < width) ? src[col] : 0.f;
+                            v[q][k] = (i < ie && k < ncol && col < width) ? src[col] : 0.f;
                         }
                     }
 #pragma unroll
                     for (int q = 0; q < kItemBatch; ++q) {
-                        const int i = i0 + q;
                         if (wq[q] == -INFINITY) continue;
                         const float wi = expf(wq[q] - M);
-                        S += ws.part_l[(int64_t)i * Hq + h] * wi;
+                        S += lq[q] * wi;
 #pragma unroll
                         for (int k = 0; k < kMaxWidthPerLane; ++k) acc[k] = fmaf(v[q][k], wi, acc[k]);
                     }
@@ -105,7 +129,8 @@ combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_
         return;
     }
     const float* wp = w + (int64_t)p * width * D;
-    if ((D & 3) == 0 && D <= 128) {
+    if (vec_w) {
+        const uint64_t keep = l2_evict_last_policy();
         const int dg = tid & 31, slice = tid >> 5;
         const int l0 = (width * slice) / kLSlices, l1 = (width * (slice + 1)) / kLSlices;
         float acc[kCombineRows][4];
@@ -116,7 +141,7 @@ combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_
         if (4 * dg < D) {
 #pragma unroll 16
             for (int l = l0; l < l1; ++l) {
-                const float4 wv = __ldg(reinterpret_cast<const float4*>(wp + (int64_t)l * D) + dg);
+                const float4 wv = ldg_f4_keep(reinterpret_cast<const float4*>(wp + (int64_t)l * D) + dg, keep);
 #pragma unroll
                 for (int r = 0; r < kCombineRows; ++r) {
                     const float c = cs[r * width + l];
