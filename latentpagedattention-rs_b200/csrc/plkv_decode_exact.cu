@@ -392,58 +392,76 @@ cudaError_t launch_fullkv_partial_exact(const plkv_fullkv_decode_args& a, Decode
 
 // ------------------------------------------------------- query projection
 
-// grid = batch * kv_heads, block = 256.  q_lat[b, kv*G + j, l] =
-// sum_d W_k[kv, l, d] * q[b, kv*G + j, d]; warp per latent row, lanes over d.
+// q_lat[b, g*G + j, l] = sum_d W_k[g, l, d] * q[b, g*G + j, d]: per KV head g
+// a GEMM of the B*G query rows (b, j) by the L latent rows of W_k[g], K = D.
+// grid = (ceil(B*G / 64), ceil(L / 32), KV), block = 256: a 64 x 32 output
+// tile, D in chunks of 32 through shared memory; each thread owns 4 rows x 2
+// columns and adds d in increasing order.  (One CTA per (b, g) with a warp
+// per latent row re-read W_k[g] for every batch row and took 47 us for
+// B = 64, 32 heads, L = 256.)
+constexpr int kPqRows = 64, kPqCols = 32, kPqK = 32;
+
 __global__ void __launch_bounds__(256)
 project_query_kernel(const float* __restrict__ q, const float* __restrict__ w_k,
-                     float* __restrict__ q_lat, int Hq, int KV, int D, int L) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    float* qs = reinterpret_cast<float*>(smem_raw);  // [G][D]
-    const int G = Hq / KV;
-    const int b = blockIdx.x / KV, g = blockIdx.x % KV;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < G * D; i += 256) qs[i] = q[((int64_t)b * Hq + g * G) * D + i];
-    __syncthreads();
-    constexpr int kMaxPerLane = 8;  // D <= 256
-    constexpr int kRows = 4;        // latent rows per warp iteration, loads in flight together
-    for (int l0 = warp; l0 < L; l0 += 8 * kRows) {
-        float wv[kRows][kMaxPerLane];
+                     float* __restrict__ q_lat, int B, int Hq, int KV, int D, int L) {
+    __shared__ float as[kPqRows][kPqK + 1];
+    __shared__ float bs_[kPqCols][kPqK + 1];
+    const int G = Hq / KV, M = B * G;
+    const int g = blockIdx.z, m0 = blockIdx.x * kPqRows, l0 = blockIdx.y * kPqCols;
+    const int tid = threadIdx.x, tm = tid >> 4, tn = tid & 15;
+    float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+    for (int d0 = 0; d0 < D; d0 += kPqK) {
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-            const int l = l0 + 8 * r;
-            const float* wr = w_k + ((int64_t)g * L + l) * D;
-#pragma unroll
-            for (int i = 0; i < kMaxPerLane; ++i) {
-                const int d = lane + 32 * i;
-                wv[r][i] = (l < L && d < D) ? wr[d] : 0.f;
+        for (int k = 0; k < kPqRows * kPqK / 256; ++k) {
+            const int i = tid + 256 * k, r = i / kPqK, dd = i % kPqK;
+            const int m = m0 + r, d = d0 + dd;
+            float v = 0.f;
+            if (m < M && d < D) {
+                const int b = m / G, j = m - b * G;
+                v = q[((int64_t)b * Hq + g * G + j) * D + d];
             }
+            as[r][dd] = v;
         }
-        for (int j = 0; j < G; ++j) {
 #pragma unroll
-            for (int r = 0; r < kRows; ++r) {
-                float acc = 0.f;
+        for (int k = 0; k < kPqCols * kPqK / 256; ++k) {
+            const int i = tid + 256 * k, c = i / kPqK, dd = i % kPqK;
+            const int l = l0 + c, d = d0 + dd;
+            bs_[c][dd] = (l < L && d < D) ? w_k[((int64_t)g * L + l) * D + d] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int dd = 0; dd < kPqK; ++dd) {
+            float a[4], w2[2];
 #pragma unroll
-                for (int i = 0; i < kMaxPerLane; ++i) {
-                    const int d = lane + 32 * i;
-                    if (d < D) acc = fmaf(wv[r][i], qs[j * D + d], acc);
-                }
-                acc = warp_sum(acc);
-                const int l = l0 + 8 * r;
-                if (lane == 0 && l < L) q_lat[((int64_t)b * Hq + g * G + j) * L + l] = acc;
-            }
+            for (int i = 0; i < 4; ++i) a[i] = as[tm * 4 + i][dd];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) w2[k] = bs_[tn * 2 + k][dd];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int k = 0; k < 2; ++k) acc[i][k] = fmaf(a[i], w2[k], acc[i][k]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + tm * 4 + i;
+        if (m >= M) continue;
+        const int b = m / G, j = m - b * G;
+        float* dst = q_lat + ((int64_t)b * Hq + g * G + j) * L;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int l = l0 + tn * 2 + k;
+            if (l < L) dst[l] = acc[i][k];
         }
     }
 }
 
 cudaError_t launch_project_query(const float* q, const float* w_k, float* q_lat, int B, int Hq,
                                  int KV, int D, int L, cudaStream_t st) {
-    const size_t smem = size_t(Hq / KV) * D * 4;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(project_query_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    project_query_kernel<<<B * KV, 256, smem, st>>>(q, w_k, q_lat, Hq, KV, D, L);
+    const int M = B * (Hq / KV);
+    dim3 grid((M + kPqRows - 1) / kPqRows, (L + kPqCols - 1) / kPqCols, KV);
+    project_query_kernel<<<grid, 256, 0, st>>>(q, w_k, q_lat, B, Hq, KV, D, L);
     return cudaGetLastError();
 }
 

@@ -109,6 +109,9 @@ def test_host_validation_before_launch():
     a.latent_dim, a.value_dim = 8, 8
     a.workspace_bytes = 1
     assert L.plkv_latent_decode(ctypes.byref(a), None) == m.PLKV_ERR_WORKSPACE
+    a.workspace_bytes, a.workspace = 1 << 30, fake + 16   # scratch must be 256-byte aligned
+    assert L.plkv_latent_decode(ctypes.byref(a), None) == m.PLKV_ERR_INVALID_ARGUMENT
+    a.workspace = fake
     assert L.plkv_project_query(fake, fake, fake, 1, 6, 4, 16, 8, None) == \
         m.PLKV_ERR_INVALID_PAGED_LOOKUP
     assert L.plkv_latent_append_f16(fake, fake, 4, None, fake, None, 1, fake, 6, 0, 8, None,
