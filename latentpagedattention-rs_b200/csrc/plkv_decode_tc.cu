@@ -92,7 +92,6 @@ constexpr int kKPer = 36 / kIssuers;                          // S k-steps per i
 // S partial p of buffer sb at 256 + 32 (kSBufs p + sb)
 __host__ __device__ constexpr uint32_t s_col(int p, int sb) { return 256u + 32u * (kSBufs * p + sb); }
 constexpr float kTau = 8.f;
-constexpr int kPrefetchTiles = 6;                             // L2 prefetch distance
 constexpr float kLn2 = 0.6931471805599453f;
 
 // Misc region: barriers (8 bytes each), then small shared arrays.
@@ -193,7 +192,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
 latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                          const __grid_constant__ CUtensorMap v_map,
                          const __grid_constant__ CUtensorMap q_map,
-                         const uint16_t* __restrict__ cache, int bs,
+                         int bs,
                          const int32_t* __restrict__ tables, int64_t max_blocks,
                          int64_t num_physical, const int32_t* __restrict__ seq_lens,
                          const plkv_work_item* __restrict__ items,
@@ -254,7 +253,13 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
     if (warp == 0) {
         // ---------------------------------------------------- Q and K loads
         if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
+            // K rows are read a second time, from L2, by the V loads of the
+            // same tile (the other CTA's token half, and this CTA's value
+            // columns), so they enter L2 with the normal eviction priority;
+            // the V loads, their last use, mark them evict-first.  K loads
+            // marked evict-first lost part of those rows before the V loads
+            // came: 352 -> 322 us per partial pass when this changed.
+            const uint64_t pol = policy_evict_normal();
             const uint32_t kfull0 = mapa(mb + kBarKFull, 0), kfull1 = mapa(mb + kBarKFull + 8, 0);
             const uint32_t qfull = mapa(mb + kBarQFull, 0);
             int gt = 0;  // tile counter over the worker's items
@@ -274,22 +279,10 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                 // The first K tiles of an item only need free K stages; Q waits
                 // for every MMA of the previous item, so load it after them.
                 const int pre = min(2, g.n_tiles);
-                // L2 prefetch of this CTA's token half of the item's first tiles;
-                // then kPrefetchTiles ahead of the K loads.  The peer prefetches
-                // the other half, so both halves of every tile reach L2 early.
-                for (int j = 0; j < min(kPrefetchTiles, g.n_tiles); ++j)
-                    prefetch_l2(cache + (int64_t)half_row(g, j, (int)rank, tables, max_blocks,
-                                                          num_physical, bs, flags) * kLatent,
-                                32 * kLatent * 2);
                 for (int j = 0; ok && j < g.n_tiles; ++j) {
                     // Block-table lookups first: their latency then overlaps
                     // the wait for a free stage instead of following it.
                     const int y = half_row(g, j, (int)rank, tables, max_blocks, num_physical, bs, flags);
-                    if (j + kPrefetchTiles < g.n_tiles)
-                        prefetch_l2(cache + (int64_t)half_row(g, j + kPrefetchTiles, (int)rank,
-                                                              tables, max_blocks, num_physical, bs,
-                                                              flags) * kLatent,
-                                    32 * kLatent * 2);
                     if (j == pre && !(ok = load_q())) break;
                     const int gj = gt + j, st = gj & 1;
                     if (gj >= 2 && !(ok = mbar_wait(mb + kBarKEmpty + 8 * st, ((gj - 2) >> 1) & 1,
@@ -727,7 +720,7 @@ cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWor
     }
     const int workers = (a.worker_item_begin && a.n_workers > 0) ? a.n_workers : a.n_items;
     tc::latent_partial_tc_kernel<<<2 * workers, 320, tc::kSmemBytes, st>>>(
-        k_map, v_map, q_map, a.cache, a.block_size, a.block_tables, a.max_blocks, a.num_physical,
+        k_map, v_map, q_map, a.block_size, a.block_tables, a.max_blocks, a.num_physical,
         a.seq_lens,
         a.items, (a.worker_item_begin && a.n_workers > 0) ? a.worker_item_begin : nullptr, ws,
         flags);
