@@ -51,10 +51,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __host__ __device__ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Workspace of one decode call: per-item partial softmax state and context,
-// per-row (sequence, head) final max / sum used to emit probabilities, and
-// the FP16 pre-scaled query the tensor-core pass loads by TMA.
+// Workspace of one decode call: per-launch control words, per-item partial
+// softmax state and context, per-row (sequence, head) final max / sum used to
+// emit probabilities, and the FP16 pre-scaled query the tensor-core pass
+// loads by TMA.
 struct DecodeWorkspace {
+    int32_t* ctl;     // [64] control words of one launch; ctl[0] = abort (zeroed per launch)
     float* part_m;    // [n_items, q_heads]   running max of the item's scores
     float* part_l;    // [n_items, q_heads]   sum of exp(score - part_m)
     float* part_ctx;  // [n_items, q_heads, width] unnormalised context
@@ -63,10 +65,12 @@ struct DecodeWorkspace {
     uint16_t* q16;    // [batch, q_heads, latent] FP16 (latent = 0: absent)
 };
 
+constexpr size_t kCtlBytes = 256;
+
 __host__ __device__ inline size_t decode_workspace_bytes(int n_items, int batch, int q_heads,
                                                          int latent, int width) {
     size_t nh = size_t(n_items) * q_heads;
-    return align256(nh * 4) * 2 + align256(nh * size_t(width) * 4) +
+    return kCtlBytes + align256(nh * 4) * 2 + align256(nh * size_t(width) * 4) +
            align256(size_t(batch) * q_heads * 4) * 2 +
            align256(size_t(batch) * q_heads * size_t(latent) * 2);
 }
@@ -76,6 +80,8 @@ inline DecodeWorkspace carve_workspace(void* base, int n_items, int batch, int q
     char* p = static_cast<char*>(base);
     size_t nh = size_t(n_items) * q_heads;
     DecodeWorkspace w;
+    w.ctl = reinterpret_cast<int32_t*>(p);
+    p += kCtlBytes;
     w.part_m = reinterpret_cast<float*>(p);
     p += align256(nh * 4);
     w.part_l = reinterpret_cast<float*>(p);

@@ -216,6 +216,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
     uint8_t* misc = smem + kMiscOff;
     const uint32_t mb = sbase + kMiscOff;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + kAbort);
+    const WaitCtx wc{flags, ws.ctl, abort_flag};
     float* red_max = reinterpret_cast<float*>(misc + kRedMax);
     float* red_sum = reinterpret_cast<float*>(misc + kRedSum);
 
@@ -269,7 +270,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                 const int ni = ii - i_begin;
                 auto load_q = [&]() -> bool {
                     if (ni >= 1 &&
-                        !mbar_wait(mb + kBarQFree, (ni - 1) & 1, flags, abort_flag))
+                        !mbar_wait(mb + kBarQFree, (ni - 1) & 1, wc))
                         return false;
                     if (leader) mbar_arrive_expect_tx(mb + kBarQFull, kQTx);
                     const int y = g.seq * kHeads + kHeadsPerCta * (int)rank;
@@ -286,7 +287,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                     if (j == pre && !(ok = load_q())) break;
                     const int gj = gt + j, st = gj & 1;
                     if (gj >= 2 && !(ok = mbar_wait(mb + kBarKEmpty + 8 * st, ((gj - 2) >> 1) & 1,
-                                                    flags, abort_flag)))
+                                                    wc)))
                         break;
                     if (leader) mbar_arrive_expect_tx(mb + kBarKFull + 8 * st, kKTx);
                     const uint32_t dst = sbase + kKOff + st * kKStage;
@@ -311,7 +312,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                     const int y0 = half_row(g, j, 0, tables, max_blocks, num_physical, bs, flags);
                     const int y1 = half_row(g, j, 1, tables, max_blocks, num_physical, bs, flags);
                     if (gj >= 2 && !(ok = mbar_wait(mb + kBarVEmpty + 8 * st, ((gj - 2) >> 1) & 1,
-                                                    flags, abort_flag)))
+                                                    wc)))
                         break;
                     mbar_arrive_expect_tx(mb + kBarVFull + 8 * st, kVTx);
                     const uint32_t dst = sbase + kVOff + st * kVStage;
@@ -433,14 +434,12 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                         next_check = now + kFlagPollNs;
                     } else if (now >= next_check) {
                         next_check = now + kFlagPollNs;
-                        if (flags && (*reinterpret_cast<volatile int32_t*>(flags) &
-                                      PLKV_FLAG_TIMEOUT)) {
+                        if (*wc.abort) {
                             *abort_flag = 1;
                             break;
                         }
                         if (now - idle_since > kWaitLimitNs) {
-                            set_flag(flags, PLKV_FLAG_TIMEOUT);
-                            *abort_flag = 1;
+                            wait_give_up(wc);
                             break;
                         }
                     }
@@ -469,7 +468,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                 const int sb = gj % kSBufs;
                 if (ok)
                     ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarSFull + 8 * sb,
-                                                           (gj / kSBufs) & 1, flags, abort_flag));
+                                                           (gj / kSBufs) & 1, wc));
                 float s[32];
                 if (ok) {
                     tc_fence_after();
@@ -522,11 +521,11 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                 l += psum;
                 if (ok && gj >= 2)  // P buffer `st` is free once O of tile gj-2 completed
                     ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * st,
-                                                           ((gj - 2) >> 1) & 1, flags, abort_flag));
+                                                           ((gj - 2) >> 1) & 1, wc));
                 if (ok && __any_sync(0xffffffffu, resc && j > 0)) {
                     const int jp = gj - 1;  // rescale O accumulated through tile gj-1
                     ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * (jp & 1),
-                                                           (jp >> 1) & 1, flags, abort_flag));
+                                                           (jp >> 1) & 1, wc));
                     if (ok) {
                         tc_fence_after();
 #pragma unroll 1
@@ -552,7 +551,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                     // The V tile of this CTA must have landed before O reads it
                     // (and before rows past the end are cleared).
                     ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarVFull + 8 * st, (gj >> 1) & 1,
-                                                           flags, abort_flag));
+                                                           wc));
                 }
                 if (ok && vc < kTile) {
                     // Rows past the end of the item: zero their value rows so
@@ -575,7 +574,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
             if (ok && g.n_tiles > 0) {
                 const int jl = gt + g.n_tiles - 1;
                 ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * (jl & 1), (jl >> 1) & 1,
-                                                       flags, abort_flag));
+                                                       wc));
             }
             red_sum[t] = l;
             named_sync_softmax();
@@ -635,9 +634,11 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
     if (warp == 1) tmem_dealloc_pair(tmem, kTmemCols);
 }
 
-// q16[b, h, l] = FP16(q_lat[b, h, l] * qscale), the TMA source of Q.
+// q16[b, h, l] = FP16(q_lat[b, h, l] * qscale), the TMA source of Q; also
+// clears the launch's control words (the partial pass follows in stream order).
 __global__ void q_prep_kernel(const float4* __restrict__ q, uint2* __restrict__ q16, float qscale,
-                              int64_t n4) {
+                              int64_t n4, int32_t* __restrict__ ctl) {
+    if (blockIdx.x == 0 && threadIdx.x < kCtlBytes / 4) ctl[threadIdx.x] = 0;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float4 v = q[i];
@@ -647,10 +648,6 @@ __global__ void q_prep_kernel(const float4* __restrict__ q, uint2* __restrict__ 
                             *reinterpret_cast<const uint32_t*>(&b));
     }
 }
-
-// Flag word used when the caller passes none: a wait that gives up must be
-// visible to the other CTA of the pair so that its waits end at once too.
-__device__ int32_t g_tc_flags;
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::once_flag g_encode_once;
@@ -707,17 +704,13 @@ cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWor
     int blocks = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
     tc::q_prep_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const float4*>(a.q_lat),
                                               reinterpret_cast<uint2*>(ws.q16),
-                                              a.scale * 1.4426950408889634f, n4);
+                                              a.scale * 1.4426950408889634f, n4, ws.ctl);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(tc::latent_partial_tc_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
     if (e != cudaSuccess) return e;
     int32_t* flags = a.err_flags;
-    if (!flags) {
-        e = cudaGetSymbolAddress(reinterpret_cast<void**>(&flags), tc::g_tc_flags);
-        if (e != cudaSuccess) return e;
-    }
     const int workers = (a.worker_item_begin && a.n_workers > 0) ? a.n_workers : a.n_items;
     tc::latent_partial_tc_kernel<<<2 * workers, 320, tc::kSmemBytes, st>>>(
         k_map, v_map, q_map, a.block_size, a.block_tables, a.max_blocks, a.num_physical,

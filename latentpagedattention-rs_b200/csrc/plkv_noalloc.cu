@@ -46,7 +46,8 @@ int scratch_address(void** out) {
 extern "C" int plkv_latent_decode_noalloc(const plkv_latent_decode_args* args,
                                           plkv_stream_t stream) {
     if (!args) return PLKV_ERR_INVALID_ARGUMENT;
-    if (args->n_items <= 0 || args->batch <= 0 || args->q_heads <= 0 || args->value_dim <= 0)
+    if (args->n_items <= 0 || args->batch <= 0 || args->q_heads <= 0 || args->latent_dim <= 0 ||
+        args->value_dim <= 0)
         return PLKV_ERR_ZERO_VALUE;
     const size_t need =
         plkv::decode_workspace_bytes(args->n_items, args->batch, args->q_heads, args->latent_dim,

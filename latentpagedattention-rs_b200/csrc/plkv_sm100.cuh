@@ -110,30 +110,49 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Where a bounded wait reports and learns of failures.  `report` is the
+// caller's error word (may be NULL): a wait that gives up ORs
+// PLKV_FLAG_TIMEOUT into it.  `abort` is a control word of this launch in
+// global memory, zeroed by the launch's first kernel: a wait that gives up
+// sets it, and every other waiting CTA of the launch (the peer of a CTA pair
+// included) sees it and gives up too.  The caller's word is never read, so an
+// old error bit left in it does not end later launches.  `local` is this
+// CTA's own flag in shared memory.
+struct WaitCtx {
+    int32_t* report;
+    volatile int32_t* abort;
+    volatile int* local;
+};
+
+__device__ __forceinline__ void wait_give_up(const WaitCtx& w) {
+    set_flag(w.report, PLKV_FLAG_TIMEOUT);
+    *w.abort = 1;
+    __threadfence();
+    *w.local = 1;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs (or soon after another wait, in this CTA or the peer, gave
-// up), records PLKV_FLAG_TIMEOUT and returns false; the caller then abandons
-// its work.  The global flag word is an L2 round trip, so it is read only
-// every kFlagPollNs of waiting: reading it between every two polls would
-// stretch each poll to that round trip and delay the waiter by as much.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* flags,
-                                          volatile int* abort_flag) {
+// kWaitLimitNs (or soon after another wait of this launch gave up) and
+// returns false; the caller then abandons its work.  The launch's abort word
+// is an L2 round trip, so it is read only every kFlagPollNs of waiting:
+// reading it between every two polls would stretch each poll to that round
+// trip and delay the waiter by as much.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtx& w) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     uint64_t next_check = t0 + kFlagPollNs;
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
+        if (*w.local) return false;
         const uint64_t now = globaltimer();
         if (now < next_check) continue;
         next_check = now + kFlagPollNs;
-        if (flags && (*reinterpret_cast<volatile int32_t*>(flags) & PLKV_FLAG_TIMEOUT)) {
-            *abort_flag = 1;
+        if (*w.abort) {
+            *w.local = 1;
             return false;
         }
         if (now - t0 > kWaitLimitNs) {
-            set_flag(flags, PLKV_FLAG_TIMEOUT);
-            *abort_flag = 1;
+            wait_give_up(w);
             return false;
         }
     }
