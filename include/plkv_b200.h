@@ -127,21 +127,29 @@ int plkv_reconstruct_kv(const void* latent, int32_t latent_is_f16, int64_t num_s
  * at index rank) and ctrl a zeroed DEVICE array of 4 uint64 of this rank.
  * Per step: plkv_peer_publish(ctx[rows, width], lse[rows]) after the rank's
  * combine, then plkv_peer_merge(out[rows, width], lse_out[rows] or NULL),
- * which waits (bounded: PLKV_FLAG_TIMEOUT, outputs 0) for every rank's
- * publish of the step and merges them with the LSE rule.  Every rank issues
- * the same sequence of steps; world <= 32.  Close and free the buffers only
- * after every rank's last merge completed (a host barrier). */
+ * which waits (bounded, 1 s: PLKV_FLAG_TIMEOUT, rows 0 and lse -inf, no peer
+ * memory read) for every rank's publish of the step and merges them with the
+ * LSE rule.  Every rank issues the same sequence of steps with the same rows
+ * and width; world <= 32.  Each buffer records its slot capacity at
+ * allocation: a step whose rows x width exceeds a buffer is refused on the
+ * device with PLKV_FLAG_BAD_POSITION (publish writes nothing, and the merges
+ * of that step then time out).  The launch grid may change between steps.
+ * Close and free the buffers only after every rank's last merge completed (a
+ * host barrier).  plkv_peer_init_buffer prepares caller-allocated device
+ * memory of `bytes` the same way (header zeroed, capacity recorded; it
+ * synchronises `stream`), for ranks that live in one process. */
 typedef struct plkv_ipc_handle {
     char bytes[64];
 } plkv_ipc_handle;
 size_t plkv_peer_buffer_bytes(int64_t rows, int32_t width);
 int plkv_peer_alloc(size_t bytes, void** ptr, plkv_ipc_handle* handle);
+int plkv_peer_init_buffer(void* buf, size_t bytes, plkv_stream_t stream);
 int plkv_peer_open(const plkv_ipc_handle* handle, void** ptr);
 int plkv_peer_close(void* ptr);
 int plkv_peer_free(void* ptr);
 int plkv_peer_publish(const float* ctx, const float* lse, int64_t rows, int32_t width,
                       void* const* bufs, int32_t world, int32_t rank, uint64_t* ctrl,
-                      plkv_stream_t stream);
+                      int32_t* err_flags, plkv_stream_t stream);
 int plkv_peer_merge(int64_t rows, int32_t width, void* const* bufs, int32_t world, int32_t rank,
                     uint64_t* ctrl, float* out, float* lse_out, int32_t* err_flags,
                     plkv_stream_t stream);
@@ -348,6 +356,19 @@ size_t plkv_fullkv_decode_workspace_size(int32_t n_items, int32_t batch, int32_t
  * and paged_gqa_decode_attention_intermediates_ref (attention_ref.py:172-224)
  * on FP16 storage, batched with a table and a length per sequence. */
 int plkv_fullkv_decode(const plkv_fullkv_decode_args* args, plkv_stream_t stream);
+
+/* ------------------------------------------------------------ diagnostics */
+
+/* Self-test of the bounded waits of the tensor-core decode on this device
+ * (no counterpart in the reference).  Two CTAs wait on a barrier that nothing
+ * completes: CTA 0 gives up after its 1 s limit, ORs PLKV_FLAG_TIMEOUT into
+ * *err_flags and sets *ctl (the launch's abort word, device memory, caller
+ * initialised); CTA 1 starts 0.5 s later and gives up as soon as it sees *ctl
+ * set.  elapsed_ns[2] (device) receives each wait's duration.  With *ctl = 1
+ * on entry both waits end within microseconds and nothing is reported.  No
+ * fault or trap is involved; the call returns after about 1 s. */
+int plkv_selftest_bounded_wait(int32_t* ctl, int64_t* elapsed_ns, int32_t* err_flags,
+                               plkv_stream_t stream);
 
 #ifdef __cplusplus
 }

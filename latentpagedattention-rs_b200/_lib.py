@@ -81,10 +81,11 @@ SIGNATURES = {
                                             _I32, _I32, _P, _P, _I32, _P, _P]),
     "plkv_peer_buffer_bytes": (_SZ, [_I64, _I32]),
     "plkv_peer_alloc": (ctypes.c_int, [_SZ, _P, _P]),
+    "plkv_peer_init_buffer": (ctypes.c_int, [_P, _SZ, _P]),
     "plkv_peer_open": (ctypes.c_int, [_P, _P]),
     "plkv_peer_close": (ctypes.c_int, [_P]),
     "plkv_peer_free": (ctypes.c_int, [_P]),
-    "plkv_peer_publish": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _I32, _I32, _P, _P]),
+    "plkv_peer_publish": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _I32, _I32, _P, _P, _P]),
     "plkv_peer_merge": (ctypes.c_int, [_I64, _I32, _P, _I32, _I32, _P, _P, _P, _P, _P]),
     "plkv_allocate_slots": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _I64, _P, _I64, _P,
                                             _P]),
@@ -103,6 +104,7 @@ SIGNATURES = {
     "plkv_out_proj": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _I32, _P, _SZ, _P]),
     "plkv_fullkv_decode_workspace_size": (_SZ, [_I32, _I32, _I32, _I32]),
     "plkv_fullkv_decode": (ctypes.c_int, [ctypes.POINTER(FullKVDecodeArgs), _P]),
+    "plkv_selftest_bounded_wait": (ctypes.c_int, [_P, _P, _P, _P]),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -10,12 +10,17 @@
 // straight from their memory.
 //
 // Buffer of rank r (allocated by r, mapped by every peer):
-//   [0, 512)            flags: uint64 epoch published by rank s at index s
+//   [0, 256)            flags: uint64 epoch published by rank s at index s
+//   [256, 264)          capacity of one slot in bytes, written at allocation
 //   [512, ...)          two slots (epoch parity) of rows x (width + 1) floats,
 //                       each padded to a multiple of 256 bytes: the rows'
 //                       contexts, then their log-sum-exps
 // Control words of rank r (local only): epoch of the last merge, and a
-// counter of finished CTAs per kernel.
+// counter of finished CTAs of the running kernel (the last CTA resets it, so
+// the grid may differ from step to step).  A step whose rows x width does not
+// fit a buffer's slots is refused on the device (PLKV_FLAG_BAD_POSITION):
+// publish then writes nothing and does not advance its flag, so the peers'
+// merges of that step end with PLKV_FLAG_TIMEOUT.
 //
 // Step e (= last epoch + 1), stream-ordered on every rank:
 //   publish: copy this rank's (ctx, lse) into its own slot e & 1; the last CTA
@@ -39,7 +44,8 @@ namespace plkv {
 namespace {
 
 constexpr int kFlagBytes = 512;
-constexpr int kMaxPeers = 32;  // one lane per rank in the merge
+constexpr int kCapOffset = 256;  // uint64 slot capacity in bytes
+constexpr int kMaxPeers = 32;    // one lane per rank in the merge
 
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -61,11 +67,21 @@ __device__ __forceinline__ float* slot(void* buf, int parity, int64_t rows, int 
                                     parity * slot_bytes(rows, width));
 }
 
+__device__ __forceinline__ bool fits(const void* buf, int64_t rows, int width) {
+    const uint64_t cap = *reinterpret_cast<const volatile uint64_t*>(
+        static_cast<const uint8_t*>(buf) + kCapOffset);
+    return (uint64_t)slot_bytes(rows, width) <= cap;
+}
+
 // grid-stride copy of (ctx, lse) into the own slot; the last CTA publishes.
 __global__ void __launch_bounds__(256)
 publish_kernel(const float* __restrict__ ctx, const float* __restrict__ lse, int64_t rows,
                int width, void* const* __restrict__ bufs, int world, int rank,
-               uint64_t* __restrict__ ctrl) {
+               uint64_t* __restrict__ ctrl, int32_t* flags) {
+    if (!fits(bufs[rank], rows, width)) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) set_flag(flags, PLKV_FLAG_BAD_POSITION);
+        return;
+    }
     const uint64_t e = ctrl[0] + 1;
     float* dst = slot(bufs[rank], (int)(e & 1), rows, width);
     const int64_t n_ctx = rows * width;
@@ -87,18 +103,22 @@ publish_kernel(const float* __restrict__ ctx, const float* __restrict__ lse, int
     if (threadIdx.x == 0) {
         const unsigned long long done =
             atomicAdd(reinterpret_cast<unsigned long long*>(ctrl + 1), 1ull);
-        last = done + 1 == e * gridDim.x;
+        last = done + 1 == gridDim.x;
+        if (last) ctrl[1] = 0;  // the next step's kernel follows in stream order
     }
     __syncthreads();
     if (last && threadIdx.x < world) {
         __threadfence_system();
-        uint64_t* flags = static_cast<uint64_t*>(bufs[threadIdx.x]);
-        st_release_sys(flags + rank, e);
+        uint64_t* pflags = static_cast<uint64_t*>(bufs[threadIdx.x]);
+        st_release_sys(pflags + rank, e);
     }
 }
 
 // one warp per row: waits for every rank's rows of this step, then merges
-// them (lane s holds rank s's weight exp(lse_s - max)).
+// them (lane s holds rank s's weight exp(lse_s - max)).  If a wait gives up
+// (PLKV_FLAG_TIMEOUT) or a buffer is too small for the step
+// (PLKV_FLAG_BAD_POSITION), no peer memory is read: the rows come out as 0
+// with log-sum-exp -inf.
 __global__ void __launch_bounds__(256)
 merge_kernel(int64_t rows, int width, void* const* __restrict__ bufs, int world, int rank,
              uint64_t* __restrict__ ctrl, float* __restrict__ out, float* __restrict__ lse_out,
@@ -107,8 +127,14 @@ merge_kernel(int64_t rows, int width, void* const* __restrict__ bufs, int world,
     const int parity = (int)(e & 1);
     __shared__ int ok_s;
     if (threadIdx.x == 0) {
-        const uint64_t* f = static_cast<const uint64_t*>(bufs[rank]);
         int ok = 1;
+        for (int s = 0; s < world && ok; ++s) {
+            if (!fits(bufs[s], rows, width)) {
+                if (blockIdx.x == 0) set_flag(flags, PLKV_FLAG_BAD_POSITION);
+                ok = 0;
+            }
+        }
+        const uint64_t* f = static_cast<const uint64_t*>(bufs[rank]);
         const uint64_t t0 = sm100::globaltimer();
         for (int s = 0; s < world && ok; ++s) {
             while (ld_acquire_sys(f + s) < e) {
@@ -124,7 +150,10 @@ merge_kernel(int64_t rows, int width, void* const* __restrict__ bufs, int world,
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * 8 + warp;
-    if (row < rows) {
+    if (row < rows && !ok_s) {
+        for (int c = lane; c < width; c += 32) out[row * width + c] = 0.f;
+        if (lse_out && lane == 0) lse_out[row] = -INFINITY;
+    } else if (row < rows) {
         const float* src_lane = lane < world ? slot(bufs[lane], parity, rows, width) : nullptr;
         const float l = src_lane ? src_lane[rows * width + row] : -INFINITY;
         float M = l;
@@ -134,7 +163,7 @@ merge_kernel(int64_t rows, int width, void* const* __restrict__ bufs, int world,
         float den = w;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-        const float inv = (ok_s && den > 0.f) ? 1.f / den : 0.f;
+        const float inv = den > 0.f ? 1.f / den : 0.f;
         // Every lane runs the same iterations (the shuffles name the whole
         // warp); only the loads and stores are guarded by the width.  The
         // sources' values of a column are all loaded before any is used, so
@@ -161,7 +190,8 @@ merge_kernel(int64_t rows, int width, void* const* __restrict__ bufs, int world,
     if (threadIdx.x == 0) {
         const unsigned long long done =
             atomicAdd(reinterpret_cast<unsigned long long*>(ctrl + 2), 1ull);
-        if (done + 1 == e * gridDim.x) {
+        if (done + 1 == gridDim.x) {
+            ctrl[2] = 0;
             __threadfence();
             ctrl[0] = e;
         }
@@ -183,7 +213,11 @@ int plkv_peer_alloc(size_t bytes, void** ptr, plkv_ipc_handle* handle) {
     void* p = nullptr;
     if (cudaMalloc(&p, bytes) != cudaSuccess) return PLKV_ERR_CUDA;
     cudaIpcMemHandle_t h;
-    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    const uint64_t cap = bytes > (size_t)plkv::kFlagBytes ? (bytes - plkv::kFlagBytes) / 2 : 0;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess ||
+        cudaMemcpy(static_cast<uint8_t*>(p) + plkv::kCapOffset, &cap, sizeof(cap),
+                   cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
         cudaFree(p);
         return PLKV_ERR_CUDA;
     }
@@ -208,9 +242,20 @@ int plkv_peer_close(void* ptr) {
 
 int plkv_peer_free(void* ptr) { return cudaFree(ptr) == cudaSuccess ? PLKV_OK : PLKV_ERR_CUDA; }
 
+int plkv_peer_init_buffer(void* buf, size_t bytes, plkv_stream_t stream) {
+    if (!buf || bytes < (size_t)plkv::kFlagBytes + 512) return PLKV_ERR_INVALID_ARGUMENT;
+    const uint64_t cap = (bytes - plkv::kFlagBytes) / 2;
+    if (cudaMemsetAsync(buf, 0, plkv::kFlagBytes, (cudaStream_t)stream) != cudaSuccess ||
+        cudaMemcpyAsync(static_cast<uint8_t*>(buf) + plkv::kCapOffset, &cap, sizeof(cap),
+                        cudaMemcpyHostToDevice, (cudaStream_t)stream) != cudaSuccess ||
+        cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess)
+        return PLKV_ERR_CUDA;
+    return PLKV_OK;
+}
+
 int plkv_peer_publish(const float* ctx, const float* lse, int64_t rows, int32_t width,
                       void* const* bufs, int32_t world, int32_t rank, uint64_t* ctrl,
-                      plkv_stream_t stream) {
+                      int32_t* err_flags, plkv_stream_t stream) {
     if (rows <= 0 || width <= 0 || world <= 0) return PLKV_ERR_ZERO_VALUE;
     if (!ctx || !lse || !bufs || !ctrl || rank < 0 || rank >= world ||
         world > plkv::kMaxPeers || (reinterpret_cast<uintptr_t>(ctx) & 15))
@@ -218,7 +263,7 @@ int plkv_peer_publish(const float* ctx, const float* lse, int64_t rows, int32_t 
     const int64_t work = rows * width / 4 + rows;
     const int grid = (int)std::min<int64_t>((work + 255) / 256, 32);
     plkv::publish_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(ctx, lse, rows, width, bufs,
-                                                                  world, rank, ctrl);
+                                                                  world, rank, ctrl, err_flags);
     return cudaGetLastError() == cudaSuccess ? PLKV_OK : PLKV_ERR_CUDA;
 }
 

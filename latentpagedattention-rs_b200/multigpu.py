@@ -212,8 +212,13 @@ class PeerExchange:
 
         from . import _lib
 
-        nbytes = int(_lib.lib().plkv_peer_buffer_bytes(rows, width))
+        L = _lib.lib()
+        nbytes = int(L.plkv_peer_buffer_bytes(rows, width))
         bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=device) for _ in range(world)]
+        stream = torch.cuda.current_stream(torch.device(device)).cuda_stream
+        for b in bufs:
+            _lib.check(L.plkv_peer_init_buffer(b.data_ptr(), nbytes, stream),
+                       "plkv_peer_init_buffer")
         ptrs = [b.data_ptr() for b in bufs]
         return [cls(rows, width, world, r, device, _local_ptrs=ptrs) for r in range(world)], bufs
 
@@ -222,7 +227,7 @@ class PeerExchange:
 
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def publish(self, ctx, lse) -> None:
+    def publish(self, ctx, lse, flags=None) -> None:
         import torch
 
         for n, t in (("ctx", ctx), ("lse", lse)):
@@ -234,7 +239,9 @@ class PeerExchange:
         L = self._lib.lib()
         self._lib.check(L.plkv_peer_publish(ctx.data_ptr(), lse.data_ptr(), self.rows, self.width,
                                             self.bufs.data_ptr(), self.world, self.rank,
-                                            self.ctrl.data_ptr(), self._stream()),
+                                            self.ctrl.data_ptr(),
+                                            None if flags is None else flags.data_ptr(),
+                                            self._stream()),
                         "plkv_peer_publish")
 
     def merge(self, out, lse_out=None, flags=None):

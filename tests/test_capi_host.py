@@ -135,11 +135,14 @@ def test_host_validation_before_launch():
     # peer exchange: buffer size, argument checks before any launch
     assert L.plkv_peer_buffer_bytes(0, 8) == 0
     assert L.plkv_peer_buffer_bytes(10, 8) == 512 + 2 * 512  # 360-byte slots padded to 512
-    assert L.plkv_peer_publish(fake, fake, 0, 8, fake, 2, 0, fake, None) == m.PLKV_ERR_ZERO_VALUE
-    assert L.plkv_peer_publish(fake, fake, 4, 8, fake, 2, 2, fake, None) == \
+    assert L.plkv_peer_publish(fake, fake, 0, 8, fake, 2, 0, fake, None, None) == \
+        m.PLKV_ERR_ZERO_VALUE
+    assert L.plkv_peer_publish(fake, fake, 4, 8, fake, 2, 2, fake, None, None) == \
         m.PLKV_ERR_INVALID_ARGUMENT
-    assert L.plkv_peer_publish(fake, fake, 4, 8, fake, 33, 0, fake, None) == \
+    assert L.plkv_peer_publish(fake, fake, 4, 8, fake, 33, 0, fake, None, None) == \
         m.PLKV_ERR_INVALID_ARGUMENT
+    assert L.plkv_peer_init_buffer(None, 4096, None) == m.PLKV_ERR_INVALID_ARGUMENT
+    assert L.plkv_peer_init_buffer(fake, 64, None) == m.PLKV_ERR_INVALID_ARGUMENT
     assert L.plkv_peer_merge(4, 8, None, 2, 0, fake, fake, None, None, None) == \
         m.PLKV_ERR_INVALID_ARGUMENT
     assert L.plkv_peer_alloc(0, None, None) == m.PLKV_ERR_INVALID_ARGUMENT
