@@ -176,66 +176,133 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- helpers
 
-def cpu_sample_rate(s, x_host: dict, seconds: float, threads: int) -> dict:
-    """Time the reference CPU path (C restatement, OpenMP) on a bounded sample.
-
-    The sample is sequence 0 with the first `heads` query heads (and their
-    projection heads), grown until one run takes about `seconds`.  Returns
-    the extrapolated time of the full step.
-    """
-    from oracle import c_ref
-
-    c_ref.build()
-    n0 = int(x_host["lens"][0])
-    group = s.group
-    heads = max(group, min(s.q_heads, threads * group))
-    heads -= heads % group
-    while True:
-        ph = heads // group
-        q_lat = x_host["q_lat"][:1, :heads]
-        w = np.ascontiguousarray(x_host["w_v_hm"][:ph].transpose(1, 0, 2).reshape(s.value_dim, -1))
-        t0 = time.perf_counter()
-        c_ref.latent_decode_batch(q_lat, x_host["cache_bits"], x_host["tables"][:1],
-                                  x_host["lens"][:1], s.block_size, s.scale, s.value_dim, w, ph,
-                                  s.head_dim, threads=threads)
-        dt = time.perf_counter() - t0
-        if dt >= 0.25 * seconds or heads >= s.q_heads:
-            break
-        heads = min(s.q_heads, heads * 2)
-    work_sample = n0 * heads
-    work_full = int(np.sum(x_host["global_lens"].astype(np.int64))) * s.q_heads
-    return {"seconds": dt, "full_seconds": dt * work_full / work_sample,
-            "sample": f"sequence 0 ({n0} tokens) x {heads} of {s.q_heads} query heads, "
-                      f"extrapolated by tokens x heads to the full step", "threads": threads}
+def host_cores() -> int:
+    """Host cores this process may run on (torchrun's OMP_NUM_THREADS=1 does
+    not limit the CPU baseline: it passes its thread count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
-def host_sample_inputs(s, x: dict, dev_tensors: bool = True) -> dict:
-    """Host copies of what the CPU sample reads (sequence 0 only)."""
+def host_compact(s, x: dict, seqs, lens) -> dict:
+    """Host copies of what the CPU path reads for sequences `seqs` (lengths
+    `lens`): their blocks gathered into a compact pool with renumbered tables,
+    the query and the weights."""
     import torch
 
     tables = x["tables"].cpu().numpy()
-    nb = int((x["global_lens"][0] + s.block_size - 1) // s.block_size)
-    used = tables[0, :nb]
-    # Compact sequence 0's blocks into a small host pool.
-    cache = x["cache"][torch.as_tensor(used, device=x["cache"].device)].contiguous()
-    bits = cache.view(torch.int16).cpu().numpy().view(np.uint16)
-    local_table = np.arange(nb, dtype=np.int32)[None]
-    if "q_lat" in x:
-        q_lat = x["q_lat"][:1].cpu().numpy()
+    nbs = [int((int(n) + s.block_size - 1) // s.block_size) for n in lens]
+    blocks = np.concatenate([tables[b, :nb] for b, nb in zip(seqs, nbs)]).astype(np.int64)
+    out = {"lens": np.asarray(lens, np.int32), "seqs": np.asarray(seqs)}
+    local = np.full((len(seqs), max(max(nbs), 1)), -1, np.int32)
+    k = 0
+    for i, nb in enumerate(nbs):
+        local[i, :nb] = np.arange(k, k + nb, dtype=np.int32)
+        k += nb
+    out["tables"] = local
+    sel = torch.as_tensor(blocks, device=x["cache"].device)
+    cache = x["cache"][sel].contiguous()
+    out["cache_bits"] = cache.view(torch.int16).cpu().numpy().view(np.uint16)
+    del cache
+    if "k_cache" in x:
+        for name in ("k_cache", "v_cache"):
+            kv = x[name][sel].contiguous()
+            out[name + "_bits"] = kv.view(torch.int16).cpu().numpy().view(np.uint16)
+    idx = torch.as_tensor(np.asarray(seqs), device=x["cache"].device)
+    if s.absorbed:
+        out["q_lat"] = x["q_lat"][idx].cpu().numpy()
     else:
-        from oracle import c_ref
-
+        out["q"] = x["q"][idx].cpu().numpy()
         wk = x["w_k"].cpu().numpy()
-        canon = wk.transpose(1, 0, 2).reshape(wk.shape[1], -1)
-        q_lat = c_ref.project_query(x["q"][0].cpu().numpy(), canon, s.kv_heads)[None]
-    return {"cache_bits": bits, "tables": local_table, "lens": x["global_lens"][:1].astype(np.int32),
-            "global_lens": x["global_lens"], "q_lat": q_lat,
-            "w_v_hm": x["w_v"].cpu().numpy()}
+        out["w_k_canonical"] = wk.transpose(1, 0, 2).reshape(wk.shape[1], -1)
+    wv = x["w_v"].cpu().numpy()
+    out["w_v_canonical"] = np.ascontiguousarray(wv.transpose(1, 0, 2).reshape(s.value_dim, -1))
+    return out
+
+
+def cpu_decode(s, h: dict, path: str, threads: int) -> None:
+    """The reference's CPU path for the compacted sequences of `h`: the C
+    restatement of crates/plkv-core/src/lib.rs:1090-1145 (direct latent
+    decode) or lib.rs:1147-1269 (full-KV baseline), OpenMP over (sequence,
+    head) on `threads` host cores."""
+    from oracle import c_ref
+
+    if path == "fullkv":
+        c_ref.fullkv_decode_batch(h["q"], h["k_cache_bits"], h["v_cache_bits"], h["tables"],
+                                  h["lens"], s.scale, threads=threads)
+        return
+    if s.absorbed:
+        q_lat = h["q_lat"]
+    else:
+        q_lat = np.stack([c_ref.project_query(q, h["w_k_canonical"], s.kv_heads)
+                          for q in h["q"]])
+    c_ref.latent_decode_batch(q_lat, h["cache_bits"], h["tables"], h["lens"], s.block_size,
+                              s.scale, s.value_dim, h["w_v_canonical"], s.proj_heads,
+                              s.head_dim, threads=threads)
+
+
+class CpuSample:
+    """A bounded sample of the workload for the CPU path: sequence 0 (all
+    query heads) cut to its first `tokens` tokens, sized so that one run
+    takes about `seconds`.  The work is linear in the tokens attended, so its
+    throughput is the full step's; `full_step()` times the whole workload
+    once to check that."""
+
+    def __init__(self, s, x: dict, path: str, threads: int, seconds: float):
+        self.s, self.x, self.path, self.threads = s, x, path, threads
+        self.n0 = int(x["global_lens"][0])
+        tokens = min(self.n0, 8 * s.block_size)
+        while True:
+            h = host_compact(s, x, [0], [tokens])
+            t0 = time.perf_counter()
+            cpu_decode(s, h, path, threads)
+            dt = time.perf_counter() - t0
+            if tokens >= self.n0 or dt >= 0.2 * seconds:
+                break
+            tokens = min(self.n0, tokens * 4)
+        want = int(tokens * seconds / max(dt, 1e-6))
+        tokens = int(np.clip(want // s.block_size * s.block_size, s.block_size, self.n0))
+        self.tokens = tokens
+        self.h = host_compact(s, x, [0], [tokens])
+        self.tokens_full = int(np.sum(x["global_lens"].astype(np.int64)))
+        self.desc = (f"sequence 0, all {s.q_heads} query heads, its first {tokens} of "
+                     f"{self.n0} tokens ({tokens / self.tokens_full:.3%} of the step's "
+                     f"{self.tokens_full} tokens)")
+
+    def run(self) -> float:
+        t0 = time.perf_counter()
+        cpu_decode(self.s, self.h, self.path, self.threads)
+        return time.perf_counter() - t0
+
+    def full_step(self, limit_s: float, sample_s: float) -> float | None:
+        """Seconds of one full step of the workload, or None when the sample
+        (`sample_s` per run) predicts more than `limit_s`."""
+        if sample_s * self.tokens_full / self.tokens > limit_s:
+            return None
+        s, x = self.s, self.x
+        h = host_compact(s, x, list(range(s.batch)), [int(n) for n in x["global_lens"]])
+        t0 = time.perf_counter()
+        cpu_decode(s, h, self.path, self.threads)
+        return time.perf_counter() - t0
 
 
 # -------------------------------------------------------------- reference arm
 
+def workload_config(s, args, tokens: int, w_o: bool, algo: int) -> dict:
+    """The workload a line measures; identical in both arms."""
+    return {"workload": s.name, "path": args.path, "batch": s.batch, "q_heads": s.q_heads,
+            "kv_heads": s.kv_heads, "latent_dim": s.latent_dim, "value_dim": s.value_dim,
+            "head_dim": s.head_dim, "block_size": s.block_size, "tokens": tokens, "w_o": w_o,
+            "l2": ("inputs larger than L2 (no flush)" if algo > 126e6
+                   else "inputs smaller than L2")}
+
+
 def run_reference(args, s, rank: int, world: int):
+    """The reference's CPU implementation of the path on the host cores.
+
+    Rank 0 alone runs it (other ranks of a torchrun launch exit), with every
+    host core it may use, on the same bounded sample at every N."""
     if rank != 0:
         return
     import torch
@@ -243,36 +310,43 @@ def run_reference(args, s, rank: int, world: int):
     dev = torch.device("cuda:0") if torch.cuda.is_available() else torch.device("cpu")
     from oracle import c_ref
 
-    threads = c_ref.max_threads()
-    # Inputs of sequence 0 are generated exactly as our arm does (device
-    # generator), then copied to the host for the CPU path.
+    c_ref.build()
+    threads = host_cores()
     wl = importlib.import_module(PACKAGE + ".workloads")
-    x = wl.device_inputs(s, dev, with_out_proj=False)
-    xh = host_sample_inputs(s, x)
+    # Inputs are generated exactly as our arm generates them (device generator).
+    x = wl.device_inputs(s, dev, with_out_proj=False, with_fullkv=args.path == "fullkv")
+    per_step_target = min(2.5, 60.0 / max(1, args.steps + args.warmup))
+    sample = CpuSample(s, x, args.path, threads, per_step_target)
+    for _ in range(args.warmup):
+        sample.run()
+    t_run0 = time.perf_counter()
+    per_step = [sample.run() for _ in range(args.steps)]
+    timed_s = time.perf_counter() - t_run0
+    t = statistics.median(per_step)
+    full_s = sample.full_step(limit_s=60.0, sample_s=t)
     del x
     torch.cuda.empty_cache()
-    per_step = []
-    r = None
-    for i in range(args.warmup + args.steps):
-        r = cpu_sample_rate(s, xh, args.cpu_seconds / max(1, args.steps), threads)
-        if i >= args.warmup:
-            per_step.append(r["full_seconds"])
-    t = statistics.median(per_step)
     lens = wl.initial_lens(s)
-    algo = wl.algorithmic_bytes(s, lens, with_out_proj=args.with_wo)
-    value = algo / t / 1e12
+    algo = wl.algorithmic_bytes(s, lens, with_out_proj=args.with_wo, fullkv=args.path == "fullkv")
+    frac = sample.tokens / sample.tokens_full
+    value = algo * frac / t / 1e12
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t * 1e3, "us_per_step": t * 1e6, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": s.name, "batch": s.batch, "q_heads": s.q_heads,
-                       "latent_dim": s.latent_dim, "value_dim": s.value_dim,
-                       "block_size": s.block_size, "tokens": int(lens.sum()),
-                       "w_o": bool(args.with_wo and s.out_dim)},
+            "config": workload_config(s, args, int(lens.sum()),
+                                      bool(args.with_wo and s.out_dim), algo),
+            "run": {"mode": "exact FP32 (CPU)", "path": args.path, "threads": threads},
+            "step_is_sample": True,
+            "timed_seconds": timed_s,
+            "full_step_ms_from_sample": t / frac * 1e3,
+            "full_step_ms_measured": None if full_s is None else full_s * 1e3,
             "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads,
-                             "kind": "port", "sample": r["sample"]},
+                             "kind": "port", "sample": sample.desc},
             "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    if full_s is not None:
+        line["full_step_value_measured"] = algo / full_s / 1e12
     print(json.dumps(line), flush=True)
 
 
@@ -299,6 +373,8 @@ def run_ours(args, s, rank: int, world: int):
     if args.path != "latent" and (s.absorbed or split_k or args.grow):
         raise SystemExit("--path fullkv / materialised: one-GPU GQA workloads with W_k, no --grow")
     D = s.head_dim
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)   # device error word of every step
+    last = {}                                               # attention-level result of a step
     # --grow: every step allocates one new token per sequence on the device;
     # room for all the steps this run takes (warm-up, eager, graph, e2e).
     grow_steps = args.warmup + 3 * args.steps + 16 if args.grow else 0
@@ -358,10 +434,14 @@ def run_ours(args, s, rank: int, world: int):
         plan = loop.plan
         launches_per_step = loop.launches_per_step
 
+        flags = loop.flags
+
         def run_step(ev=None):
             if ev is not None:
                 loop.partial_events = [ev]
-            return loop.step()[0]
+            r = loop.step()[0]
+            last["ctx"] = loop.ctx[0]
+            return r
     elif args.path != "latent":
         # Comparison points on the same shapes: stored FP16 K/V ("fullkv": the
         # step appends K/V rows and decodes them) and K/V rebuilt from the
@@ -399,9 +479,10 @@ def run_ours(args, s, rank: int, world: int):
 
         def step(q_src, rows_src, ev=None):
             if args.path == "fullkv":
-                ops.kv_append(k_rows, v_rows, k_cache, v_cache, tables, positions=positions)
+                ops.kv_append(k_rows, v_rows, k_cache, v_cache, tables, positions=positions,
+                              flags=flags)
             else:
-                ops.latent_append(rows_src, x["cache"], tables, positions=positions)
+                ops.latent_append(rows_src, x["cache"], tables, positions=positions, flags=flags)
                 rev = None
                 if ev is not None:
                     rev = (torch.cuda.Event(enable_timing=True),
@@ -409,16 +490,17 @@ def run_ours(args, s, rank: int, world: int):
                     rec_events.append(rev)
                     rev[0].record()
                 ops.reconstruct_kv(x["cache"], x["w_k"], x["w_v"], slots=act_slots,
-                                   block_size=bs, k_out=k_cache, v_out=v_cache)
+                                   block_size=bs, k_out=k_cache, v_out=v_cache, flags=flags)
                 if rev is not None:
                     rev[1].record()
             if ev is not None:
                 ev[0].record()
             ops.fullkv_decode(q_src, k_cache, v_cache, tables, lens, plan, scale=s.scale,
-                              out=ctx, workspace=fws)
+                              out=ctx, workspace=fws, flags=flags)
             if ev is not None:
                 ev[1].record()
             res = ctx
+            last["ctx"] = ctx
             if w_o is not None:
                 res = ops.out_proj(res.reshape(nb_local, -1), w_o, out=out, k_splits=wo_splits,
                                    workspace=wo_ws)
@@ -447,6 +529,8 @@ def run_ours(args, s, rank: int, world: int):
                                    device=dev) if split_k and peer_x is None else None
         gathered_lse = torch.empty((world, nb_local, s.q_heads), dtype=torch.float32,
                                    device=dev) if split_k and peer_x is None else None
+        merged_nccl = (torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
+                       if split_k and peer_x is None else None)
         K_o = s.q_heads * D
         if wo_sharded:
             # rows projected on every rank: the merged contexts (split-K) or
@@ -476,30 +560,31 @@ def run_ours(args, s, rank: int, world: int):
 
         def step(q_src, rows_src, ev=None):
             if split_k:
-                ops.latent_append_slots(rows_src, x["cache"], slots_d)
+                ops.latent_append_slots(rows_src, x["cache"], slots_d, flags=flags)
             else:
-                ops.latent_append(rows_src, x["cache"], tables, positions=positions)
+                ops.latent_append(rows_src, x["cache"], tables, positions=positions, flags=flags)
             q_lat = q_src if s.absorbed else ops.project_query(q_src, x["w_k"], out=q_lat_buf)
             if ev is not None:
                 ev[0].record()
             r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
                                   value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
                                   want_lse=want_lse, workspace=ws, allow_empty=split_k,
-                                  phase="partial")
+                                  flags=flags, phase="partial")
             if ev is not None:
                 ev[1].record()
             r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
                                   value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
                                   want_lse=want_lse, workspace=ws, allow_empty=split_k,
-                                  phase="combine")
+                                  flags=flags, phase="combine")
             res = ctx
             if split_k and peer_x is not None:
-                peer_x.publish(ctx, r["lse"])
-                res = peer_x.merge(merged)
+                peer_x.publish(ctx, r["lse"], flags=flags)
+                res = peer_x.merge(merged, flags=flags)
             elif split_k:
                 res = mg.gather_and_merge(ctx, r["lse"], world,
-                                          lambda c, l: ops.lse_merge(c, l)[0],
+                                          lambda c, l: ops.lse_merge(c, l, out=merged_nccl)[0],
                                           gathered_ctx, gathered_lse)
+            last["ctx"] = res
             if w_o is not None and wo_sharded:
                 rows = (res.reshape(B, -1) if split_k else
                         mg.gather_rows(res.reshape(nb_local, -1), world, max_rows,
@@ -564,19 +649,23 @@ def run_ours(args, s, rank: int, world: int):
             loop.capture()
 
             def stepper():
-                return loop.step()[0]
+                r = loop.step()[0]
+                last["ctx"] = loop.ctx[0]
+                return r
         else:
-            # With split-K the step holds the NCCL all-gather of the shards'
-            # (context, lse); every rank captures the same sequence, after the
-            # eager steps above have set up the communicator.
+            # With split-K the step holds the exchange of the shards' (context,
+            # lse); every rank captures the same sequence, after the eager
+            # steps above have set up the communicator.
             torch.cuda.synchronize(dev)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, capture_error_mode="thread_local"):
                 g_res = step(q_buf, rows_buf)
+            g_ctx = last["ctx"]
             barrier()
 
             def stepper():
                 graph.replay()
+                last["ctx"] = g_ctx
                 return g_res
         for _ in range(3):
             stepper()
@@ -604,42 +693,38 @@ def run_ours(args, s, rank: int, world: int):
     attended_global = (global_lens.astype(np.int64)
                        + (timed_from + args.steps // 2 if args.grow else 0))
 
-    # End to end through the public API with host buffers: H2D of the step's
-    # query and new rows, the step, D2H of the result.
+    # End to end with host buffers: every step copies its query and new rows
+    # from pinned host memory and reads its result back; the next step's
+    # host-to-device copy and this step's device-to-host copy run on a copy
+    # stream beside the step.
     e2e = None
     if not args.no_e2e:
-        q_host = q_buf.cpu().pin_memory()
-        rows_host = rows_buf.cpu().pin_memory()
-        res0 = stepper()
-        steps_done += 1
-        res_host = torch.empty(tuple(res0.shape), dtype=torch.float32).pin_memory()
-        for _ in range(2):
-            q_buf.copy_(q_host, non_blocking=True)
-            rows_buf.copy_(rows_host, non_blocking=True)
-            res_host.copy_(stepper(), non_blocking=True)
         barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
         n_e2e = max(3, args.steps // 2)
-        e0.record()
-        for _ in range(n_e2e):
-            q_buf.copy_(q_host, non_blocking=True)
-            rows_buf.copy_(rows_host, non_blocking=True)
-            res_host.copy_(stepper(), non_blocking=True)
-        e1.record()
-        barrier()
-        te = torch.tensor([e0.elapsed_time(e1) / n_e2e], dtype=torch.float64, device=dev)
+        e2e_ms, h2d, d2h = e2e_pipelined(stepper, q_buf, rows_buf, n_e2e, dev)
+        steps_done += n_e2e + 3
+        te = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        hb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e_ms = float(te[0])
-        h2d = q_host.numel() * 4 + rows_host.numel() * 4
-        d2h = res_host.numel() * 4
-        if world > 1:
-            hb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
             dist.all_reduce(hb)
-            h2d, d2h = int(hb[0]), int(hb[1])
-        e2e = {"ms_per_step": e2e_ms, "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h)}
+        e2e = {"ms_per_step": float(te[0]), "h2d_bytes_per_step": int(hb[0]),
+               "d2h_bytes_per_step": int(hb[1])}
+
+    # Parity of the last step's result against an FP64 restatement of the
+    # path (torch, on the device) over the attended rows of sampled
+    # sequences, gathered from every rank under split-K.  Outside timing.
+    res_last = stepper()
+    torch.cuda.synchronize(dev)
+    parity = check_parity(s, x, mode, world, rank, dev, split_k, seqs, global_lens,
+                          lens_host, tables, last["ctx"], res_last, w_o, wo_sharded,
+                          loop if args.grow else None,
+                          (k_cache, v_cache) if args.path != "latent" else None,
+                          max_rows if (wo_sharded and not split_k) else 0)
+    err = torch.tensor([float(int(flags.item()))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    err_flags = int(err.item())
 
     if graph is not None:
         # A graph that holds NCCL calls must be released before the process
@@ -691,22 +776,18 @@ def run_ours(args, s, rank: int, world: int):
             "scaling": "strong", "vs_baseline": None,
             "dtype": "f32" if mode == "exact" else "f16",
             "data": "synthetic (seeded, device-generated)",
-            "config": {"workload": s.name, "mode": mode, **path_info, "batch": s.batch,
-                       "q_heads": s.q_heads, "latent_dim": s.latent_dim,
-                       "value_dim": s.value_dim, "head_dim": D, "block_size": s.block_size,
-                       "tokens": int(attended_global.sum()), "w_o": w_o is not None,
-                       "cuda_graph": bool(args.graph),
-                       "ms_per_step_eager": eager_ms / args.steps,
-                       "growing": ("one token per sequence allocated on the device each step"
-                                   if args.grow else "no: the append rewrites the last token"),
-                       "exchange": (args.exchange if split_k else None),
-                       "parallelism": (f"split-k{world}" if split_k else
-                                       (f"dp{world}" if world > 1 else "single")),
-                       "l2": "inputs larger than L2 (no flush)" if algo > 126e6
-                             else "inputs smaller than L2",
-                       "work_items": plan.n_items},
+            "config": workload_config(s, args, int(attended_global.sum()), w_o is not None,
+                                      algo),
+            "run": {"mode": mode, **path_info, "cuda_graph": bool(args.graph),
+                    "ms_per_step_eager": eager_ms / args.steps,
+                    "growing": ("one token per sequence allocated on the device each step"
+                                if args.grow else "no: the append rewrites the last token"),
+                    "exchange": (args.exchange if split_k else None),
+                    "parallelism": (f"split-k{world}" if split_k else
+                                    (f"dp{world}" if world > 1 else "single")),
+                    "work_items": plan.n_items},
             "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
-            "clocks": clock_info,
+            "clocks": clock_info, "parity": parity, "err_flags": err_flags,
             # persistent cache of the attended tokens: the latent pool against the
             # FP16 K/V pool the same heads would need (memory_model.py)
             "cache_bytes": importlib.import_module(PACKAGE + ".memory_model").cache_bytes_report(
@@ -716,17 +797,204 @@ def run_ours(args, s, rank: int, world: int):
         line["e2e"] = {"value": algo / (e2e["ms_per_step"] * 1e-3) / 1e12, "unit": "TB/s",
                        "ms_per_step": e2e["ms_per_step"],
                        "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
-                       "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]}
+                       "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
+                       "copies": "pinned host buffers; the next step's H2D and this step's "
+                                 "D2H overlap the step on a copy stream"}
     if world == 1 and not args.no_cpu_baseline:
         from oracle import c_ref
 
-        xh = host_sample_inputs(s, x)
-        r = cpu_sample_rate(s, xh, args.cpu_seconds, c_ref.max_threads())
-        line["cpu_baseline"] = {"value": algo / r["full_seconds"] / 1e12, "unit": "TB/s",
-                                "cores": r["threads"], "kind": "port", "sample": r["sample"],
-                                "full_step_seconds_extrapolated": r["full_seconds"]}
+        c_ref.build()
+        threads = host_cores()
+        xs = dict(x)
+        xs["global_lens"] = global_lens
+        if args.path == "fullkv":
+            xs["k_cache"], xs["v_cache"] = k_cache, v_cache
+        sample = CpuSample(s, xs, "fullkv" if args.path == "fullkv" else "latent", threads,
+                           min(10.0, args.cpu_seconds))
+        t_cpu = statistics.median(sample.run() for _ in range(2))
+        frac = sample.tokens / sample.tokens_full
+        line["cpu_baseline"] = {"value": algo * frac / t_cpu / 1e12, "unit": "TB/s",
+                                "cores": threads, "kind": "port", "sample": sample.desc,
+                                "full_step_ms_from_sample": t_cpu / frac * 1e3}
     return line
 
+
+def e2e_pipelined(stepper, q_dst, rows_dst, n_steps: int, dev):
+    """Times `n_steps` steps end to end: each step's query and new rows come
+    from pinned host memory and its result goes back to pinned host memory.
+    The inputs are double-buffered on the device, so step i+1's host-to-device
+    copy and step i's device-to-host copy run on a copy stream while step i
+    computes; the step copies its staged inputs into the static buffers it
+    reads.  Returns (ms per step, H2D bytes, D2H bytes per step)."""
+    import torch
+
+    comp = torch.cuda.current_stream(dev)
+    cs = torch.cuda.Stream(dev)
+    q_host = [q_dst.cpu().pin_memory() for _ in range(2)]
+    r_host = [rows_dst.cpu().pin_memory() for _ in range(2)]
+    q_stage = [torch.empty_like(q_dst) for _ in range(2)]
+    r_stage = [torch.empty_like(rows_dst) for _ in range(2)]
+    res0 = stepper()
+    res_stage = [torch.empty_like(res0) for _ in range(2)]
+    res_host = [torch.empty(tuple(res0.shape), dtype=res0.dtype).pin_memory() for _ in range(2)]
+    h2d_done = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    d2h_done = [torch.cuda.Event() for _ in range(2)]
+
+    def h2d(k):
+        with torch.cuda.stream(cs):
+            q_stage[k].copy_(q_host[k], non_blocking=True)
+            r_stage[k].copy_(r_host[k], non_blocking=True)
+            h2d_done[k].record(cs)
+
+    def run(n):
+        cs.wait_stream(comp)
+        h2d(0)
+        for i in range(n):
+            k = i & 1
+            if i + 1 < n:
+                if i >= 1:
+                    cs.wait_event(consumed[1 - k])   # step i-1 has read that stage
+                h2d(1 - k)
+            comp.wait_event(h2d_done[k])
+            q_dst.copy_(q_stage[k], non_blocking=True)
+            rows_dst.copy_(r_stage[k], non_blocking=True)
+            consumed[k].record(comp)
+            res = stepper()
+            if i >= 2:
+                comp.wait_event(d2h_done[k])         # step i-2's result has left that stage
+            res_stage[k].copy_(res, non_blocking=True)
+            out_ready[k].record(comp)
+            cs.wait_event(out_ready[k])
+            with torch.cuda.stream(cs):
+                res_host[k].copy_(res_stage[k], non_blocking=True)
+                d2h_done[k].record(cs)
+        comp.wait_stream(cs)
+
+    run(2)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    run(n_steps)
+    e1.record(comp)
+    torch.cuda.synchronize(dev)
+    h2d_bytes = q_dst.numel() * q_dst.element_size() + rows_dst.numel() * rows_dst.element_size()
+    d2h_bytes = res0.numel() * res0.element_size()
+    return e0.elapsed_time(e1) / n_steps, h2d_bytes, d2h_bytes
+
+
+def _ref_latent_ctx(s, q_lat64, rows16, w_v):
+    """FP64 restatement of the direct latent decode of one sequence
+    (attention_ref.py:617-648): scores of the attended rows, softmax,
+    latent context, per-head value projection."""
+    import torch
+
+    r = rows16.double()
+    sc = (q_lat64 @ r.T) * s.scale
+    p = torch.softmax(sc, dim=1)
+    c = p @ r[:, :s.value_dim]
+    w = w_v.double()
+    group = s.q_heads // w.shape[0]
+    if group > 1:
+        w = w.repeat_interleave(group, dim=0)
+    return torch.einsum("hl,hld->hd", c, w)
+
+
+def _ref_fullkv_ctx(s, q64, k16, v16):
+    """FP64 restatement of the full-KV paged GQA decode of one sequence
+    (lib.rs:1147-1269): k16 / v16 token-major [n, KV, D]."""
+    import torch
+
+    KV, D = k16.shape[1], k16.shape[2]
+    G = s.q_heads // KV
+    q = q64.view(KV, G, D)
+    sc = torch.einsum("kgd,tkd->kgt", q, k16.double()) * s.scale
+    p = torch.softmax(sc, dim=2)
+    return torch.einsum("kgt,tkd->kgd", p, v16.double()).reshape(s.q_heads, D)
+
+
+def check_parity(s, x, mode, world, rank, dev, split_k, seqs, global_lens, lens_host,
+                 tables, ctx_res, res, w_o, wo_sharded, loop, kv, max_rows):
+    """Normwise relative error max|a - e| / max|e| of sampled sequences'
+    results against the FP64 restatement; max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    mg = importlib.import_module(PACKAGE + ".multigpu")
+    tol = 2e-3 if mode == "tc" else 1e-5
+    bs = s.block_size
+    cur_tables = loop.tables if loop is not None else tables
+    cur_lens = (loop.seq_lens.cpu().numpy() if loop is not None else lens_host).astype(np.int64)
+    errs, errs_wo, checked = [], [], []
+    if split_k:
+        # every rank holds a range of every sequence's blocks: gather them
+        counts = np.stack([mg.split_k_ranges(global_lens, bs, world, r, s.steps - 1)[1]
+                           for r in range(world)])                 # [world, B]
+        sample = sorted({0, s.batch - 1})
+    else:
+        sample = sorted({0, len(seqs) - 1}) if len(seqs) else []
+    for i in sample:
+        if split_k:
+            cnt = counts[:, i]
+            mx = int(cnt.max())
+            send = torch.zeros((mx, bs, s.latent_dim), dtype=torch.float16, device=dev)
+            mine = int(cnt[rank])
+            if mine:
+                send[:mine] = x["cache"][tables[i, :mine].long()]
+            got = torch.empty((world, mx, bs, s.latent_dim), dtype=torch.float16, device=dev)
+            dist.all_gather_into_tensor(got, send)
+            rows = torch.cat([got[r, :int(cnt[r])] for r in range(world)]).reshape(-1, s.latent_dim)
+            n = int(global_lens[i])
+            b_global = i
+        else:
+            n = int(cur_lens[i])
+            nb = (n + bs - 1) // bs
+            blk = cur_tables[i, :nb].long()
+            b_global = int(seqs[i])
+            if kv is None:
+                rows = x["cache"][blk].reshape(-1, s.latent_dim)
+        if kv is not None:
+            kc, vc = kv
+            k16 = kc[blk].permute(0, 2, 1, 3).reshape(-1, s.kv_heads, s.head_dim)[:n]
+            v16 = vc[blk].permute(0, 2, 1, 3).reshape(-1, s.kv_heads, s.head_dim)[:n]
+            q_src = (loop.q[0] if loop is not None else x["q"][torch.as_tensor(seqs, device=dev)])
+            ref = _ref_fullkv_ctx(s, q_src[i].double(), k16, v16)
+        else:
+            rows = rows[:n]
+            if s.absorbed:
+                q_src = loop.q[0] if loop is not None else x["q_lat"]
+                q64 = q_src[i if loop is not None else b_global].double()
+            else:
+                q_src = loop.q[0] if loop is not None else x["q"]
+                wk = x["w_k"].double().repeat_interleave(s.q_heads // s.kv_heads, dim=0)
+                q64 = torch.einsum("hd,hld->hl",
+                                   q_src[i if loop is not None else b_global].double(), wk)
+            ref = _ref_latent_ctx(s, q64, rows, x["w_v"])
+        got_ctx = ctx_res[i].double()
+        errs.append(float((got_ctx - ref).abs().max() / ref.abs().max()))
+        checked.append(int(b_global))
+        if w_o is not None:
+            ref_out = ref.reshape(1, -1) @ w_o.double()
+            if wo_sharded:
+                row = i if split_k else rank * max_rows + i
+                got_out = res[rank, row].double()
+            else:
+                got_out = res[i].double()
+            errs_wo.append(float((got_out - ref_out[0]).abs().max() / ref_out.abs().max()))
+    e = torch.tensor([max(errs, default=0.0), max(errs_wo, default=0.0)], dtype=torch.float64,
+                     device=dev)
+    if world > 1:
+        dist.all_reduce(e, op=dist.ReduceOp.MAX)
+    out = {"ref": "FP64 restatement of the path (torch) over the attended rows"
+                  + (", gathered from every rank" if split_k else ""),
+           "sequences": checked, "max_rel_err": float(e[0]), "tol": tol,
+           "ok": bool(float(e[0]) <= tol)}
+    if w_o is not None:
+        out["w_o_max_rel_err"] = float(e[1])
+        out["ok"] = out["ok"] and float(e[1]) <= tol
+    return out
 
 
 def run_kernel_suite(args) -> dict:
@@ -948,6 +1216,10 @@ def main():
             os.close(saved_stdout)
     if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
+        if line.get("err_flags") or not line.get("parity", {}).get("ok", True):
+            print(f"bench: the step's result failed its checks (device error flags "
+                  f"0x{line.get('err_flags', 0):x}, parity {line.get('parity')})", file=sys.stderr)
+            sys.exit(3)
 
 
 if __name__ == "__main__":
