@@ -354,7 +354,8 @@ size_t plkv_fullkv_decode_workspace_size(int32_t n_items, int32_t batch, int32_t
 /* FP16 full-KV paged GQA decode.  Replaces
  * paged_full_kv_gqa_decode_fp16_storage_runtime_f32_accum (lib.rs:1147-1269)
  * and paged_gqa_decode_attention_intermediates_ref (attention_ref.py:172-224)
- * on FP16 storage, batched with a table and a length per sequence. */
+ * on FP16 storage, batched with a table and a length per sequence.  The K and
+ * V caches must be 16-byte aligned (PLKV_ERR_UNSUPPORTED otherwise). */
 int plkv_fullkv_decode(const plkv_fullkv_decode_args* args, plkv_stream_t stream);
 
 /* ------------------------------------------------------------ diagnostics */

@@ -385,6 +385,8 @@ int plkv_fullkv_decode(const plkv_fullkv_decode_args* a, plkv_stream_t stream) {
     if (a->probs && !a->scores) return PLKV_ERR_INVALID_ARGUMENT;
     if (a->head_dim % 8 || a->head_dim > 256 || a->q_heads / a->kv_heads > 8)
         return PLKV_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(a->k_cache) | reinterpret_cast<uintptr_t>(a->v_cache)) & 15)
+        return PLKV_ERR_UNSUPPORTED;  // rows are copied in 16-byte pieces
     if ((int64_t)a->max_blocks * a->block_size > 0x7fffffffLL) return PLKV_ERR_ARITHMETIC_OVERFLOW;
     if (a->workspace_bytes <
         decode_workspace_bytes(a->n_items, a->batch, a->q_heads, 0, a->head_dim))

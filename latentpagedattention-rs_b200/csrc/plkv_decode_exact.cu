@@ -220,9 +220,34 @@ cudaError_t launch_latent_partial_exact(const plkv_latent_decode_args& a, Decode
 
 // --------------------------------------------------------------- full KV
 
-// grid = (n_items, kv_heads), block = 256.  Warp w < G owns query head
-// kv*G + w; lane = token for the scores, lane owns columns 4*lane + 128*c of
-// the context.  K and V tiles of 32 tokens are staged in FP32.
+constexpr int kKvStages = 5;    // 32-token K/V tiles in flight per CTA
+constexpr int kKvPad = 8;       // FP16 padding per staged row (16 bytes)
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                 ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+                   "l"(gmem_src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// grid = (n_items, kv_heads), block = 256, two CTAs per SM.  The item's K and
+// V rows of KV head g stream through a ring of kKvStages 32-token tiles:
+// every thread issues 16-byte asynchronous copies (cp.async) of its share of
+// a tile's rows, kKvStages - 1 tiles ahead of the one being computed, so the
+// HBM latency is covered by the tiles in flight instead of being paid per
+// tile.  Rows land as FP16 with a 16-byte pad (a 272-byte row stride for
+// D = 128), so that 32 lanes reading 16-byte chunks of 32 different rows, or
+// of one row, hit distinct banks; they are converted to FP32 as they are read.
+// Warp w < G owns query head kv*G + w: lane = token for the scores (FP32 sum
+// over d in increasing order, lib.rs:1222-1230), warp-shuffle max / sum for
+// the online softmax, then lane = 4 value columns (+128 c) for the context.
 template <int NCH>
 __global__ void __launch_bounds__(256, 2)
 fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restrict__ k_cache,
@@ -232,13 +257,13 @@ fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restr
                             const plkv_work_item* __restrict__ items, DecodeWorkspace ws,
                             float* __restrict__ scores, int max_seq_len, int32_t* flags) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int DP = D + 4;
+    const int DP = D + 4;                 // FP32 query row
+    const int RS = D + kKvPad;            // FP16 staged row
     const int G = Hq / KV;
-    float* qs = reinterpret_cast<float*>(smem_raw);  // [8][DP]
-    float* kt = qs + 8 * DP;                          // [32][DP]
-    float* vt = kt + kTileTokens * DP;                // [32][DP]
-    float* ps = vt + kTileTokens * DP;                // [32][8]
-    __shared__ int64_t row_off[kTileTokens];
+    float* qs = reinterpret_cast<float*>(smem_raw);                   // [8][DP]
+    float* ps = qs + 8 * DP;                                          // [32][8]
+    uint16_t* ring = reinterpret_cast<uint16_t*>(ps + kTileTokens * 8);  // [stages][2][32][RS]
+    __shared__ int64_t row_off[kKvStages][kTileTokens];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const plkv_work_item it = items[blockIdx.x];
@@ -250,72 +275,92 @@ fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restr
         len = len < 0 ? 0 : (int)cap;
     }
     const int t_begin = it.block_begin * bs;
-    const int t_end = min(it.block_end * bs, len);
+    const int t_end = max(t_begin, min(it.block_end * bs, len));
+    const int n_tiles = (t_end - t_begin + kTileTokens - 1) / kTileTokens;
     const bool active = warp < G;
     const int h = g * G + warp;
+    const int cpr = D >> 3;               // 16-byte chunks per row
 
     for (int i = tid; i < 8 * D; i += 256) {
         int w = i / D, d = i - w * D;
         qs[w * DP + d] = (w < G) ? q[((int64_t)b * Hq + g * G + w) * D + d] : 0.f;
     }
+
+    // Issues the copies of tile j into ring slot j % kKvStages (nothing past
+    // the item).  Each thread resolves the rows it copies through the table;
+    // thread t < 32 also records row t's offset for the compute warps.
+    auto issue = [&](int j) {
+        if (j >= n_tiles) return;
+        const int st = j % kKvStages;
+        const int t0 = t_begin + j * kTileTokens;
+        const int nt = min(kTileTokens, t_end - t0);
+        uint16_t* kdst = ring + (size_t)st * 2 * kTileTokens * RS;
+        uint16_t* vdst = kdst + kTileTokens * RS;
+        for (int i = tid; i < kTileTokens * cpr; i += 256) {
+            const int r = i / cpr, c = i - r * cpr;
+            int64_t off = -1;
+            if (r < nt) {
+                const int t = t0 + r;
+                const int lb = t / bs;
+                const int32_t phys = tables[(int64_t)b * max_blocks + lb];
+                if (phys >= 0 && phys < num_physical)
+                    off = (((int64_t)phys * KV + g) * bs + (t - lb * bs)) * (int64_t)D;
+                else if (c == 0)
+                    set_flag(flags, PLKV_FLAG_BAD_BLOCK);
+            }
+            if (c == 0) row_off[st][r] = off;
+            if (off >= 0) {
+                cp_async16(kdst + r * RS + c * 8, k_cache + off + c * 8);
+                cp_async16(vdst + r * RS + c * 8, v_cache + off + c * 8);
+            }
+        }
+    };
+
     float m_run = -INFINITY, l_run = 0.f, acc[NCH][4];
 #pragma unroll
     for (int c = 0; c < NCH; ++c)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
 
-    const int cpr = D >> 3;
-    for (int t0 = t_begin; t0 < t_end; t0 += kTileTokens) {
+#pragma unroll 1
+    for (int j = 0; j < kKvStages - 1; ++j) {
+        issue(j);
+        cp_async_commit();
+    }
+#pragma unroll 1
+    for (int j = 0; j < n_tiles; ++j) {
+        issue(j + kKvStages - 1);
+        cp_async_commit();
+        cp_async_wait<kKvStages - 1>();   // this thread's copies of tile j landed
+        __syncthreads();                   // everyone's did (and the query is staged)
+        const int st = j % kKvStages;
+        const int t0 = t_begin + j * kTileTokens;
         const int nt = min(kTileTokens, t_end - t0);
-        __syncthreads();
-        if (tid < kTileTokens) {
-            int64_t off = -1;
-            if (tid < nt) {
-                int t = t0 + tid;
-                int lb = t / bs;
-                int32_t phys = tables[(int64_t)b * max_blocks + lb];
-                if (phys >= 0 && phys < num_physical)
-                    off = (((int64_t)phys * KV + g) * bs + (t - lb * bs)) * (int64_t)D;
-                else
-                    set_flag(flags, PLKV_FLAG_BAD_BLOCK);
-            }
-            row_off[tid] = off;
-        }
-        __syncthreads();
-        for (int i = tid; i < 2 * kTileTokens * cpr; i += 256) {
-            const int which = i / (kTileTokens * cpr);
-            const int rem = i - which * kTileTokens * cpr;
-            const int r = rem / cpr, c = rem - r * cpr;
-            float v[8];
-            const int64_t off = row_off[r];
-            if (off >= 0) {
-                const uint16_t* base = which ? v_cache : k_cache;
-                uint4 raw = __ldg(reinterpret_cast<const uint4*>(base + off) + c);
-                unpack8(raw, v);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = 0.f;
-            }
-            float4* dst = reinterpret_cast<float4*>((which ? vt : kt) + r * DP + c * 8);
-            dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-            dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-        }
-        __syncthreads();
+        const uint16_t* kt = ring + (size_t)st * 2 * kTileTokens * RS;
+        const uint16_t* vt = kt + kTileTokens * RS;
         if (active) {
+            const bool tok_ok = lane < nt && row_off[st][lane] >= 0;
             float s = 0.f;
-            const float* kr = kt + lane * DP;
-            const float* qr = qs + warp * DP;
+            if (tok_ok) {
+                const uint16_t* kr = kt + lane * RS;
+                const float* qr = qs + warp * DP;
 #pragma unroll 4
-            for (int d = 0; d < D; d += 4) {
-                float4 x = *reinterpret_cast<const float4*>(kr + d);
-                float4 qv = *reinterpret_cast<const float4*>(qr + d);
-                s = fmaf(qv.x, x.x, s);
-                s = fmaf(qv.y, x.y, s);
-                s = fmaf(qv.z, x.z, s);
-                s = fmaf(qv.w, x.w, s);
+                for (int c = 0; c < cpr; ++c) {
+                    float x[8];
+                    unpack8(*reinterpret_cast<const uint4*>(kr + c * 8), x);
+                    const float4 q0 = *reinterpret_cast<const float4*>(qr + c * 8);
+                    const float4 q1 = *reinterpret_cast<const float4*>(qr + c * 8 + 4);
+                    s = fmaf(q0.x, x[0], s);
+                    s = fmaf(q0.y, x[1], s);
+                    s = fmaf(q0.z, x[2], s);
+                    s = fmaf(q0.w, x[3], s);
+                    s = fmaf(q1.x, x[4], s);
+                    s = fmaf(q1.y, x[5], s);
+                    s = fmaf(q1.z, x[6], s);
+                    s = fmaf(q1.w, x[7], s);
+                }
             }
             const float sc = s * scale;
-            const bool tok_ok = lane < nt && row_off[lane] >= 0;
             if (scores && lane < nt && t0 + lane < max_seq_len)
                 scores[((int64_t)b * Hq + h) * max_seq_len + t0 + lane] = sc;
             const float sv = tok_ok ? sc : -INFINITY;
@@ -332,20 +377,25 @@ fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restr
                 for (int e = 0; e < 4; ++e) acc[c][e] *= alpha;
             for (int r = 0; r < nt; ++r) {
                 const float pr = ps[r * 8 + warp];
-                const float* vr = vt + r * DP + lane * 4;
+                if (pr == 0.f) continue;   // masked token: its row may be stale
+                const uint16_t* vr = vt + r * RS + lane * 4;
 #pragma unroll
                 for (int c = 0; c < NCH; ++c) {
                     if (lane * 4 + 128 * c < D) {
-                        const float4 x = *reinterpret_cast<const float4*>(vr + 128 * c);
-                        acc[c][0] = fmaf(pr, x.x, acc[c][0]);
-                        acc[c][1] = fmaf(pr, x.y, acc[c][1]);
-                        acc[c][2] = fmaf(pr, x.z, acc[c][2]);
-                        acc[c][3] = fmaf(pr, x.w, acc[c][3]);
+                        const uint2 raw = *reinterpret_cast<const uint2*>(vr + 128 * c);
+                        const float2 x01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                        const float2 x23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                        acc[c][0] = fmaf(pr, x01.x, acc[c][0]);
+                        acc[c][1] = fmaf(pr, x01.y, acc[c][1]);
+                        acc[c][2] = fmaf(pr, x23.x, acc[c][2]);
+                        acc[c][3] = fmaf(pr, x23.y, acc[c][3]);
                     }
                 }
             }
         }
+        __syncthreads();   // slot st is rewritten by the next iteration's issue
     }
+    cp_async_wait<0>();
     if (!active) return;
     const int64_t row = (int64_t)blockIdx.x * Hq + h;
     if (lane == 0) {
@@ -363,7 +413,8 @@ fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restr
 }
 
 size_t fullkv_exact_smem_bytes(int D) {
-    return size_t(8 + 2 * kTileTokens) * (D + 4) * 4 + size_t(kTileTokens) * 8 * 4;
+    return size_t(8) * (D + 4) * 4 + size_t(kTileTokens) * 8 * 4 +
+           size_t(kKvStages) * 2 * kTileTokens * (D + kKvPad) * 2;
 }
 
 template <int NCH>
