@@ -302,6 +302,34 @@ int plkv_latent_decode_combine(const plkv_latent_decode_args* args, plkv_stream_
  * call reads before writing. */
 int plkv_latent_decode_noalloc(const plkv_latent_decode_args* args, plkv_stream_t stream);
 
+/* ---- Head-sharded split-K merge through peer memory (one node, NVLink) ----
+ * No counterpart in the reference (its decode is single-device).  Under
+ * split-K each rank decodes its range of every sequence's blocks with
+ * plkv_latent_decode_partial; instead of the combine, plkv_shard_publish
+ * merges the rank's work items per (sequence, head) into a normalised latent
+ * context and log-sum-exp and stores them into the buffer of the rank that
+ * owns the head (rank r owns heads [r H/W, (r+1) H/W)).  plkv_shard_merge
+ * then waits (bounded, 1 s: PLKV_FLAG_TIMEOUT, rows 0 and lse -inf) for every
+ * rank's publish of the step, merges the W sources with the LSE rule and
+ * applies W_v / W_uv of the owned heads: out[batch, H/W, head_dim] and
+ * lse_out[batch, H/W] (may be NULL) hold the merged result of this rank's
+ * heads; w_v NULL writes the latent context (width value_dim).  Buffers of
+ * plkv_shard_buffer_bytes(batch, q_heads, value_dim) bytes come from
+ * plkv_peer_alloc / plkv_peer_open (or plkv_peer_init_buffer) and are used as
+ * described for the peer exchange above: bufs a DEVICE array of the W base
+ * pointers, ctrl a zeroed DEVICE array of 4 uint64 of this rank, every rank
+ * issuing the same steps with the same shapes; q_heads % world == 0; world
+ * <= 32; value_dim <= 640.  publish reads args->workspace (the partial pass's
+ * results), seq_item_begin, batch, q_heads, latent_dim, value_dim, n_items
+ * and err_flags. */
+size_t plkv_shard_buffer_bytes(int32_t batch, int32_t q_heads, int32_t value_dim);
+int plkv_shard_publish(const plkv_latent_decode_args* args, void* const* bufs, int32_t world,
+                       int32_t rank, uint64_t* ctrl, plkv_stream_t stream);
+int plkv_shard_merge(void* const* bufs, int32_t world, int32_t rank, uint64_t* ctrl,
+                     int32_t batch, int32_t q_heads, int32_t value_dim, const float* w_v,
+                     int32_t head_dim, float* out, float* lse_out, int32_t* err_flags,
+                     plkv_stream_t stream);
+
 /* Log-sum-exp merge of per-shard results (split-K across GPUs):
  * ctx_shards [n_shards, rows, width] are normalised partial contexts and
  * lse_shards [n_shards, rows] their log-sum-exp (-inf = empty shard).

@@ -105,6 +105,11 @@ SIGNATURES = {
     "plkv_fullkv_decode_workspace_size": (_SZ, [_I32, _I32, _I32, _I32]),
     "plkv_fullkv_decode": (ctypes.c_int, [ctypes.POINTER(FullKVDecodeArgs), _P]),
     "plkv_selftest_bounded_wait": (ctypes.c_int, [_P, _P, _P, _P]),
+    "plkv_shard_buffer_bytes": (_SZ, [_I32, _I32, _I32]),
+    "plkv_shard_publish": (ctypes.c_int, [ctypes.POINTER(LatentDecodeArgs), _P, _I32, _I32, _P,
+                                          _P]),
+    "plkv_shard_merge": (ctypes.c_int, [_P, _I32, _I32, _P, _I32, _I32, _I32, _P, _I32, _P, _P,
+                                        _P, _P]),
 }
 
 _LIB: ctypes.CDLL | None = None

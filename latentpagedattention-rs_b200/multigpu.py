@@ -183,7 +183,7 @@ class PeerExchange:
         if _local_ptrs is not None:
             ptrs = list(_local_ptrs)
         else:
-            nbytes = int(L.plkv_peer_buffer_bytes(self.rows, self.width))
+            nbytes = self._buffer_bytes()
             own = ctypes.c_void_p()
             handle = (ctypes.c_char * 64)()
             _lib.check(L.plkv_peer_alloc(nbytes, ctypes.byref(own), handle), "plkv_peer_alloc")
@@ -202,6 +202,9 @@ class PeerExchange:
                 ptrs.append(p.value)
         self.bufs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
         self.ctrl = torch.zeros(4, dtype=torch.int64, device=self.device)
+
+    def _buffer_bytes(self) -> int:
+        return int(self._lib.lib().plkv_peer_buffer_bytes(self.rows, self.width))
 
     @classmethod
     def local_group(cls, world: int, rows: int, width: int, device):
@@ -276,3 +279,84 @@ class PeerExchange:
         if self.own is not None:
             L.plkv_peer_free(self.own)
         self.opened, self.own = [], None
+
+
+# ------------------------------------- head-sharded split-K merge (peer memory)
+
+class ShardExchange(PeerExchange):
+    """Head-sharded merge of split-K results (``plkv_shard_publish`` /
+    ``plkv_shard_merge``).
+
+    Rank r owns query heads ``[r * H / W, (r + 1) * H / W)``.  After the
+    partial pass, ``publish(args)`` merges the rank's work items per
+    (sequence, head) and stores the normalised latent context and its
+    log-sum-exp into the owner's buffer over NVLink; ``merge(out)`` waits for
+    every rank's publish of the step, merges the W sources and applies W_uv of
+    the owned heads.  Every rank reads W_uv for H / W heads only, and the
+    result stays sharded by heads (``out [B, H / W, D]``), the layout a
+    row-sharded W_o consumes.  Same lifetime rules as ``PeerExchange``."""
+
+    def __init__(self, batch: int, q_heads: int, value_dim: int, world: int, rank: int, device,
+                 group=None, _local_ptrs=None):
+        from . import _lib
+
+        if q_heads % world:
+            raise ValueError(f"q_heads {q_heads} is not a multiple of the world size {world}")
+        self.batch, self.q_heads, self.value_dim = int(batch), int(q_heads), int(value_dim)
+        self._nbytes = int(_lib.lib().plkv_shard_buffer_bytes(batch, q_heads, value_dim))
+        super().__init__(1, 1, world, rank, device, group=group, _local_ptrs=_local_ptrs)
+
+    def _buffer_bytes(self) -> int:
+        return self._nbytes
+
+    @property
+    def heads_per_rank(self) -> int:
+        return self.q_heads // self.world
+
+    @classmethod
+    def local_group(cls, world: int, batch: int, q_heads: int, value_dim: int, device):
+        """`world` exchanges over plain buffers of one device (a single-process
+        stand-in for the ranks, for tests): publishes must all precede the
+        merges in stream order.  Returns (exchanges, buffers)."""
+        import torch
+
+        from . import _lib
+
+        L = _lib.lib()
+        nbytes = int(L.plkv_shard_buffer_bytes(batch, q_heads, value_dim))
+        bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=device) for _ in range(world)]
+        stream = torch.cuda.current_stream(torch.device(device)).cuda_stream
+        for b in bufs:
+            _lib.check(L.plkv_peer_init_buffer(b.data_ptr(), nbytes, stream),
+                       "plkv_peer_init_buffer")
+        ptrs = [b.data_ptr() for b in bufs]
+        return [cls(batch, q_heads, value_dim, world, r, device, _local_ptrs=ptrs)
+                for r in range(world)], bufs
+
+    def publish(self, decode_args) -> None:
+        """``decode_args``: the ``LatentDecodeArgs`` of the rank's partial pass
+        (its workspace holds the work items' results)."""
+        import ctypes
+
+        L = self._lib.lib()
+        self._lib.check(L.plkv_shard_publish(ctypes.byref(decode_args), self.bufs.data_ptr(),
+                                             self.world, self.rank, self.ctrl.data_ptr(),
+                                             self._stream()), "plkv_shard_publish")
+
+    def merge(self, out, w_v=None, lse_out=None, flags=None):
+        import torch
+
+        hpr = self.heads_per_rank
+        width = self.value_dim if w_v is None else int(w_v.shape[2])
+        if not (isinstance(out, torch.Tensor) and out.is_cuda and out.dtype == torch.float32
+                and out.is_contiguous() and out.numel() == self.batch * hpr * width):
+            raise TypeError("out must be a contiguous FP32 CUDA tensor of batch x heads/world x "
+                            "width")
+        L = self._lib.lib()
+        self._lib.check(L.plkv_shard_merge(
+            self.bufs.data_ptr(), self.world, self.rank, self.ctrl.data_ptr(), self.batch,
+            self.q_heads, self.value_dim, None if w_v is None else w_v.data_ptr(),
+            0 if w_v is None else int(w_v.shape[2]), out.data_ptr(),
+            None if lse_out is None else lse_out.data_ptr(),
+            None if flags is None else flags.data_ptr(), self._stream()), "plkv_shard_merge")
+        return out

@@ -419,7 +419,8 @@ def latent_decode(q_lat: torch.Tensor, cache: torch.Tensor, block_tables: torch.
     fn = {"all": lib().plkv_latent_decode, "partial": lib().plkv_latent_decode_partial,
           "combine": lib().plkv_latent_decode_combine}[phase]
     check(fn(ctypes.byref(a), _stream(dev)), "plkv_latent_decode")
-    return {"ctx": out, "lse": lse, "scores": scores, "probs": probs, "workspace": workspace}
+    return {"ctx": out, "lse": lse, "scores": scores, "probs": probs, "workspace": workspace,
+            "args": a}
 
 
 def fullkv_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,

@@ -145,3 +145,80 @@ def test_ipc_exchange_two_processes(tmp_path):
         assert p.exitcode == 0
     res = json.loads(out.read_text())
     assert res["err"] <= 1e-5 and res["flags"] == 0
+
+
+def _mla_shards(seed, lens, world, bs=64):
+    """Absorbed-MLA inputs and each stand-in rank's share of every sequence's
+    blocks (contiguous ranges, as the split-K runner cuts them)."""
+    rng = np.random.default_rng(seed)
+    L, Lv, Hq, D = 576, 512, 128, 128
+    nb = [(n + bs - 1) // bs for n in lens]
+    P = sum(nb) + 2
+    perm = rng.permutation(P).astype(np.int32)
+    tables = np.full((len(lens), max(nb)), -1, np.int32)
+    k = 0
+    for b, c in enumerate(nb):
+        tables[b, :c] = perm[k:k + c]
+        k += c
+    lens = np.asarray(lens, np.int32)
+    shards = []
+    nbv = np.asarray(nb)
+    for r in range(world):
+        lo, hi = nbv * r // world, nbv * (r + 1) // world
+        tab = np.full_like(tables, -1)
+        local = np.zeros_like(lens)
+        for b in range(len(lens)):
+            tab[b, :hi[b] - lo[b]] = tables[b, lo[b]:hi[b]]
+            local[b] = max(0, min(lens[b], hi[b] * bs) - lo[b] * bs)
+        shards.append((tab, local))
+    return dict(cache=(rng.standard_normal((P, bs, L), dtype=np.float32) * 0.5).astype(np.float16),
+                q_lat=rng.standard_normal((len(lens), Hq, L), dtype=np.float32),
+                w_uv=(rng.standard_normal((Hq, Lv, D), dtype=np.float32)
+                      / np.float32(np.sqrt(Lv))),
+                tables=tables, lens=lens, shards=shards, bs=bs, Lv=Lv, Hq=Hq, D=D)
+
+
+@pytest.mark.parametrize("world,mode", [(2, "exact"), (4, "exact"), (8, "exact"), (4, "tc")])
+def test_head_sharded_merge_equals_unsplit_decode(world, mode):
+    """Split-K over `world` stand-in ranks on one GPU: each rank's partial pass
+    over its block ranges, head-sharded publish into the owners' buffers,
+    merge + W_uv of the owned heads; the heads concatenated equal the
+    unsplit decode (exact: 1e-5, tensor-core: 2e-3) over two steps."""
+    ops = importlib.import_module(PACKAGE + ".ops")
+    mg = _mg()
+    dev = torch.device("cuda")
+    m = _mla_shards(7 + world, [5000, 1300, 64, 2049], world)
+    t = lambda a: torch.as_tensor(np.ascontiguousarray(a), device=dev)
+    q, cache, w = t(m["q_lat"]), t(m["cache"]), t(m["w_uv"])
+    scale = 1 / np.sqrt(m["D"])
+    full = ops.latent_decode(q, cache, t(m["tables"]), t(m["lens"]),
+                             ops.plan_splits(m["lens"], m["bs"]), scale=scale, value_dim=m["Lv"],
+                             w_v=w, want_lse=True)
+    B, Hq, D = len(m["lens"]), m["Hq"], m["D"]
+    exch, _bufs = mg.ShardExchange.local_group(world, B, Hq, m["Lv"], dev)
+    hpr = Hq // world
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    for _step in range(2):
+        parts = []
+        for r, (tab, local) in enumerate(m["shards"]):
+            plan = (ops.plan_workers(local, m["bs"], n_workers=3) if mode == "tc"
+                    else ops.plan_splits(local, m["bs"]))
+            rr = ops.latent_decode(q, cache, t(tab), t(local), plan, scale=scale,
+                                   value_dim=m["Lv"], w_v=w, mode=mode, allow_empty=True,
+                                   flags=flags, phase="partial")
+            parts.append(rr)
+            exch[r].publish(rr["args"])
+        outs, lses = [], []
+        for r in range(world):
+            o = torch.empty((B, hpr, D), dtype=torch.float32, device=dev)
+            ls = torch.empty((B, hpr), dtype=torch.float32, device=dev)
+            exch[r].merge(o, w_v=w, lse_out=ls, flags=flags)
+            outs.append(o)
+            lses.append(ls)
+        torch.cuda.synchronize()
+        assert int(flags.item()) == 0
+        got = torch.cat(outs, dim=1).cpu()
+        got_lse = torch.cat(lses, dim=1).cpu()
+        tol = 2e-3 if mode == "tc" else 1e-5
+        assert rel_err(got, full["ctx"].cpu()) <= tol
+        assert rel_err(got_lse, full["lse"].cpu()) <= tol
