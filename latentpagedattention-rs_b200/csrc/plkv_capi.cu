@@ -5,6 +5,7 @@
 // GQA mapping 962-969, active length 1106-1111); the status codes are the
 // PlkvError variants of lib.rs:12-18 (include/plkv_b200.h).
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -24,6 +25,9 @@ cudaError_t launch_latent_partial_exact(const plkv_latent_decode_args&, DecodeWo
 cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args&, DecodeWorkspace,
                                      cudaStream_t);
 bool tc_supported(const plkv_latent_decode_args&);
+cudaError_t launch_latent_partial_tc2(const plkv_latent_decode_args&, DecodeWorkspace,
+                                      cudaStream_t);
+bool tc2_supported(const plkv_latent_decode_args&);
 cudaError_t launch_fullkv_partial_exact(const plkv_fullkv_decode_args&, DecodeWorkspace,
                                         cudaStream_t);
 cudaError_t launch_project_query(const float*, const float*, float*, int, int, int, int, int,
@@ -307,8 +311,14 @@ int plkv_latent_decode_partial(const plkv_latent_decode_args* a, plkv_stream_t s
                                          a->latent_dim, a->value_dim);
     cudaError_t e;
     if (a->mode == PLKV_MODE_TC_F16) {
-        if (!tc_supported(*a)) return PLKV_ERR_UNSUPPORTED;
-        e = launch_latent_partial_tc(*a, ws, (cudaStream_t)stream);
+        static const bool v1 = getenv("PLKV_TC_V1") != nullptr;  // A/B against the old pass
+        if (v1) {
+            if (!tc_supported(*a)) return PLKV_ERR_UNSUPPORTED;
+            e = launch_latent_partial_tc(*a, ws, (cudaStream_t)stream);
+        } else {
+            if (!tc2_supported(*a)) return PLKV_ERR_UNSUPPORTED;
+            e = launch_latent_partial_tc2(*a, ws, (cudaStream_t)stream);
+        }
     } else {
         e = launch_latent_partial_exact(*a, ws, (cudaStream_t)stream);
     }

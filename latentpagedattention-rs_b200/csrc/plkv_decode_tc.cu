@@ -673,6 +673,11 @@ static bool encode_f16(CUtensorMap* map, const void* base, int rank, const cuuin
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                    const cuuint64_t* strides, const cuuint32_t* box) {
+    return load_encode() && encode_f16(map, base, rank, dims, strides, box);
+}
+
 }  // namespace tc
 
 bool tc_supported(const plkv_latent_decode_args& a) {

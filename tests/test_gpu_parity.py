@@ -389,13 +389,13 @@ def test_tensor_core_matches_exact_mode(ops, pkg, workers):
     assert rel_err(lt[fin], le[fin]) <= TC_REL
 
 
-@pytest.mark.parametrize("workers,bs", [(0, 64), (3, 64), (3, 32), (5, 128)])
+@pytest.mark.parametrize("workers,bs", [(0, 64), (3, 64), (3, 256), (5, 128)])
 def test_tensor_core_ignores_nonfinite_slots_past_the_end(ops, pkg, workers, bs):
     """Pool slots past a sequence's length (the rest of its last block, and
     blocks no table names) hold NaN and Inf: the tensor-core pass reads whole
     row groups there but must weigh them by exactly zero, as the exact pass,
-    which never reads them, does.  Block sizes 32 / 64 / 128 take the three
-    TMA box heights."""
+    which never reads them, does.  Block sizes 64 / 128 / 256 place a tile's
+    pages at every offset inside a block."""
     lens = [777, 131, 4101, 64, 33, 320]
     m = _mla_case(pkg, len(lens), lens, seed=17, bs=bs)
     cache = m["cache"].reshape(-1, m["L"])          # [P * bs, L] view
@@ -416,6 +416,15 @@ def test_tensor_core_ignores_nonfinite_slots_past_the_end(ops, pkg, workers, bs)
     assert torch.isfinite(outs["tc"]["ctx"]).all() and torch.isfinite(outs["tc"]["lse"]).all()
     assert rel_err(outs["tc"]["ctx"].cpu(), outs["exact"]["ctx"].cpu()) <= TC_REL
     assert rel_err(outs["tc"]["lse"].cpu(), outs["exact"]["lse"].cpu()) <= TC_REL
+
+
+def test_tensor_core_rejects_block_size_32(ops, pkg):
+    """The tensor-core pass loads one 64-row block per CTA and tile."""
+    m = _mla_case(pkg, 1, [100], seed=3, bs=32)
+    plan = ops.plan_workers(m["lens"], m["bs"])
+    with pytest.raises(Exception, match="unsupported"):
+        ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]), t(m["lens"]), plan,
+                          scale=m["scale"], value_dim=m["Lv"], w_v=t(m["w_uv"]), mode="tc")
 
 
 def test_tensor_core_rejects_intermediates(ops, pkg):
