@@ -78,8 +78,10 @@ def parse_args():
     ap.add_argument("--path", default="latent", choices=["latent", "fullkv", "materialised"],
                     help="latent: the direct latent decode; fullkv: stored FP16 K/V; "
                          "materialised: K/V rebuilt from the latent pool every step")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
-                    help="split-K result exchange: peer memory over NVLink (two kernels) or "
+    ap.add_argument("--exchange", default="shard", choices=["shard", "peer", "nccl"],
+                    help="split-K result exchange: head-sharded merge over peer memory (each "
+                         "rank ends with its heads' rows), all heads over peer memory (two "
+                         "kernels) or "
                          "NCCL all-gathers and a merge kernel")
     ap.add_argument("--kernel-suite", action="store_true",
                     help="time every kernel of the library on one synthetic case each")
@@ -403,13 +405,20 @@ def run_ours(args, s, rank: int, world: int):
     else:
         positions = torch.as_tensor(gpos.astype(np.int32), device=dev)
     w_o = x.get("w_o")
-    # W_o column-sharded across ranks: this rank keeps out_dim / world columns.
+    # Head-sharded split-K results: W_o row-sharded, this rank keeps the rows
+    # of its heads and the partial outputs are summed.  Otherwise W_o is
+    # column-sharded: this rank keeps out_dim / world columns.
+    shard_x_on = split_k and args.exchange == "shard"
     wo_sharded = w_o is not None and world > 1
     if wo_sharded:
         if args.grow:
             raise SystemExit("--with-wo on several GPUs: not with --grow")
-        c0, c1 = mg.column_range(s.out_dim, world, rank)
-        w_o = w_o[:, c0:c1].contiguous()
+        if shard_x_on:
+            hpr_d = s.q_heads // world * D
+            w_o = w_o[rank * hpr_d:(rank + 1) * hpr_d].contiguous()
+        else:
+            c0, c1 = mg.column_range(s.out_dim, world, rank)
+            w_o = w_o[:, c0:c1].contiguous()
         x["w_o"] = None
         torch.cuda.empty_cache()
     if args.grow:
@@ -521,18 +530,26 @@ def run_ours(args, s, rank: int, world: int):
                                                     s.latent_dim, s.value_dim),
                          dtype=torch.uint8, device=dev)
         want_lse = split_k
+        shard_x = (mg.ShardExchange(nb_local, s.q_heads, s.value_dim, world, rank, dev)
+                   if shard_x_on else None)
+        res_shard = (torch.empty((nb_local, s.q_heads // world, D), dtype=torch.float32,
+                                 device=dev) if shard_x is not None else None)
         peer_x = (mg.PeerExchange(nb_local * s.q_heads, D, world, rank, dev)
                   if split_k and args.exchange == "peer" else None)
         merged = (torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
                   if peer_x is not None else None)
+        nccl_x = split_k and args.exchange == "nccl"
         gathered_ctx = torch.empty((world, nb_local, s.q_heads, D), dtype=torch.float32,
-                                   device=dev) if split_k and peer_x is None else None
+                                   device=dev) if nccl_x else None
         gathered_lse = torch.empty((world, nb_local, s.q_heads), dtype=torch.float32,
-                                   device=dev) if split_k and peer_x is None else None
+                                   device=dev) if nccl_x else None
         merged_nccl = (torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
-                       if split_k and peer_x is None else None)
+                       if nccl_x else None)
         K_o = s.q_heads * D
-        if wo_sharded:
+        max_rows = 0
+        if wo_sharded and shard_x is not None:
+            out = torch.empty((nb_local, s.out_dim), dtype=torch.float32, device=dev)
+        elif wo_sharded:
             # rows projected on every rank: the merged contexts (split-K) or
             # every rank's sequences, gathered into equal padded blocks
             max_rows = (B if split_k else
@@ -572,6 +589,15 @@ def run_ours(args, s, rank: int, world: int):
                                   flags=flags, phase="partial")
             if ev is not None:
                 ev[1].record()
+            if shard_x is not None:
+                # head-sharded merge: this rank's heads only, W_uv of those heads
+                shard_x.publish(r["args"])
+                res = shard_x.merge(res_shard, w_v=x["w_v"], flags=flags)
+                last["ctx"] = res
+                if w_o is not None:
+                    res = project(res.reshape(nb_local, -1), w_o)
+                    dist.all_reduce(res)
+                return res
             r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
                                   value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
                                   want_lse=want_lse, workspace=ws, allow_empty=split_k,
@@ -603,7 +629,9 @@ def run_ours(args, s, rank: int, world: int):
         # combine, query projection, shard merge (peer exchange: publish +
         # merge), W_o GEMM + split reduction
         launches_per_step = (3 + (mode == "tc") + (0 if s.absorbed else 1)
-                             + ((2 if peer_x is not None else 1) if split_k else 0)
+                             + ((2 if peer_x is not None or shard_x is not None else 1)
+                                if split_k else 0)
+                             - (1 if shard_x is not None else 0)
                              + (2 if w_o is not None else 0))
 
     def barrier():
@@ -720,7 +748,10 @@ def run_ours(args, s, rank: int, world: int):
                           lens_host, tables, last["ctx"], res_last, w_o, wo_sharded,
                           loop if args.grow else None,
                           (k_cache, v_cache) if args.path != "latent" else None,
-                          max_rows if (wo_sharded and not split_k) else 0)
+                          max_rows if (wo_sharded and not split_k) else 0,
+                          (rank * (s.q_heads // world), (rank + 1) * (s.q_heads // world))
+                          if (args.path == "latent" and not args.grow and shard_x is not None)
+                          else None)
     err = torch.tensor([float(int(flags.item()))], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(err, op=dist.ReduceOp.MAX)
@@ -732,8 +763,10 @@ def run_ours(args, s, rank: int, world: int):
         torch.cuda.synchronize(dev)
         graph.reset()
         graph = None
-    if not args.grow and args.path == "latent" and peer_x is not None:
-        peer_x.close()
+    if not args.grow and args.path == "latent":
+        for ex in (peer_x, shard_x):
+            if ex is not None:
+                ex.close()
     if rank != 0:
         return None
     peaks, peak_kind = load_peaks()
@@ -916,7 +949,7 @@ def _ref_fullkv_ctx(s, q64, k16, v16):
 
 
 def check_parity(s, x, mode, world, rank, dev, split_k, seqs, global_lens, lens_host,
-                 tables, ctx_res, res, w_o, wo_sharded, loop, kv, max_rows):
+                 tables, ctx_res, res, w_o, wo_sharded, loop, kv, max_rows, head_range=None):
     """Normwise relative error max|a - e| / max|e| of sampled sequences'
     results against the FP64 restatement; max over ranks."""
     import torch
@@ -973,9 +1006,21 @@ def check_parity(s, x, mode, world, rank, dev, split_k, seqs, global_lens, lens_
                                    q_src[i if loop is not None else b_global].double(), wk)
             ref = _ref_latent_ctx(s, q64, rows, x["w_v"])
         got_ctx = ctx_res[i].double()
-        errs.append(float((got_ctx - ref).abs().max() / ref.abs().max()))
+        if head_range is not None:
+            # this rank holds the merged rows of its heads only
+            h0, h1 = head_range
+            errs.append(float((got_ctx - ref[h0:h1]).abs().max() / ref.abs().max()))
+        else:
+            errs.append(float((got_ctx - ref).abs().max() / ref.abs().max()))
         checked.append(int(b_global))
-        if w_o is not None:
+        if w_o is not None and head_range is not None:
+            # W_o row-sharded by heads: the reference output is the sum of the
+            # ranks' partial products
+            ref_out = ref[h0:h1].reshape(1, -1) @ w_o.double()
+            dist.all_reduce(ref_out)
+            errs_wo.append(float((res[i].double() - ref_out[0]).abs().max()
+                                 / ref_out.abs().max()))
+        elif w_o is not None:
             ref_out = ref.reshape(1, -1) @ w_o.double()
             if wo_sharded:
                 row = i if split_k else rank * max_rows + i

@@ -264,6 +264,7 @@ fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restr
     float* ps = qs + 8 * DP;                                          // [32][8]
     uint16_t* ring = reinterpret_cast<uint16_t*>(ps + kTileTokens * 8);  // [stages][2][32][RS]
     __shared__ int64_t row_off[kKvStages][kTileTokens];
+    __shared__ int32_t ptab[kKvStages][kTileTokens];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const plkv_work_item it = items[blockIdx.x];
@@ -286,28 +287,35 @@ fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restr
         qs[w * DP + d] = (w < G) ? q[((int64_t)b * Hq + g * G + w) * D + d] : 0.f;
     }
 
+    // Physical block of every token of tile j (-1: past the item or a table
+    // entry outside the pool), kept in shared memory kKvStages tiles ahead
+    // so that issuing a tile's copies never waits on a table read.
+    auto table_of = [&](int j, int r) -> int32_t {
+        const int t = t_begin + j * kTileTokens + r;
+        if (j >= n_tiles || t >= t_end) return -1;
+        const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
+        if (phys < 0 || phys >= num_physical) {
+            if (g == 0) set_flag(flags, PLKV_FLAG_BAD_BLOCK);
+            return -1;
+        }
+        return phys;
+    };
+
     // Issues the copies of tile j into ring slot j % kKvStages (nothing past
-    // the item).  Each thread resolves the rows it copies through the table;
-    // thread t < 32 also records row t's offset for the compute warps.
+    // the item); thread t < 32 also records row t's offset for the compute
+    // warps.
     auto issue = [&](int j) {
         if (j >= n_tiles) return;
         const int st = j % kKvStages;
         const int t0 = t_begin + j * kTileTokens;
-        const int nt = min(kTileTokens, t_end - t0);
         uint16_t* kdst = ring + (size_t)st * 2 * kTileTokens * RS;
         uint16_t* vdst = kdst + kTileTokens * RS;
         for (int i = tid; i < kTileTokens * cpr; i += 256) {
             const int r = i / cpr, c = i - r * cpr;
-            int64_t off = -1;
-            if (r < nt) {
-                const int t = t0 + r;
-                const int lb = t / bs;
-                const int32_t phys = tables[(int64_t)b * max_blocks + lb];
-                if (phys >= 0 && phys < num_physical)
-                    off = (((int64_t)phys * KV + g) * bs + (t - lb * bs)) * (int64_t)D;
-                else if (c == 0)
-                    set_flag(flags, PLKV_FLAG_BAD_BLOCK);
-            }
+            const int32_t phys = ptab[st][r];
+            const int t = t0 + r;
+            const int64_t off =
+                phys < 0 ? -1 : (((int64_t)phys * KV + g) * bs + (t - (t / bs) * bs)) * (int64_t)D;
             if (c == 0) row_off[st][r] = off;
             if (off >= 0) {
                 cp_async16(kdst + r * RS + c * 8, k_cache + off + c * 8);
@@ -315,24 +323,30 @@ fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restr
             }
         }
     };
-
     float m_run = -INFINITY, l_run = 0.f, acc[NCH][4];
 #pragma unroll
     for (int c = 0; c < NCH; ++c)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[c][e] = 0.f;
 
+    for (int i = tid; i < kKvStages * kTileTokens; i += 256)
+        ptab[i / kTileTokens][i % kTileTokens] = table_of(i / kTileTokens, i % kTileTokens);
+    __syncthreads();
 #pragma unroll 1
     for (int j = 0; j < kKvStages - 1; ++j) {
         issue(j);
         cp_async_commit();
     }
+    const bool loader = warp == 7;   // reads the table entries of tile j + kKvStages
 #pragma unroll 1
     for (int j = 0; j < n_tiles; ++j) {
         issue(j + kKvStages - 1);
         cp_async_commit();
         cp_async_wait<kKvStages - 1>();   // this thread's copies of tile j landed
         __syncthreads();                   // everyone's did (and the query is staged)
+        // ptab slot j % kKvStages was last read by issue(j); refill it with
+        // tile j + kKvStages, whose copies are issued two iterations later.
+        const int32_t nxt = loader ? table_of(j + kKvStages, lane) : -1;
         const int st = j % kKvStages;
         const int t0 = t_begin + j * kTileTokens;
         const int nt = min(kTileTokens, t_end - t0);
@@ -393,6 +407,7 @@ fullkv_partial_exact_kernel(const float* __restrict__ q, const uint16_t* __restr
                 }
             }
         }
+        if (loader) ptab[j % kKvStages][lane] = nxt;
         __syncthreads();   // slot st is rewritten by the next iteration's issue
     }
     cp_async_wait<0>();

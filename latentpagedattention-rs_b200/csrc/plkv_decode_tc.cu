@@ -138,15 +138,15 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap
           "l"(policy)
         : "memory");
 }
-// The four value column blocks {z0, z0+1, z0+4, z0+5} of 32 rows in one
-// instruction: 4-D view (64 columns, rows, 4 blocks at 128 B, 2 groups of
-// blocks at 512 B); completes on a barrier of this CTA.
-__device__ __forceinline__ void tma_load_4d_own(uint32_t dst, const CUtensorMap* map, int y, int z0,
-                                                uint32_t bar, uint64_t policy) {
+// The four value column blocks [z0, z0 + 4) of 32 rows in one instruction:
+// 3-D view (64 columns, rows, 8 blocks at 128 B), one 512-byte run per row;
+// completes on a barrier of this CTA.
+__device__ __forceinline__ void tma_load_v_own(uint32_t dst, const CUtensorMap* map, int y, int z0,
+                                               uint32_t bar, uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z0), "r"(0), "r"(bar),
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z0), "r"(bar),
           "l"(policy)
         : "memory");
 }
@@ -317,7 +317,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                     mbar_arrive_expect_tx(mb + kBarVFull + 8 * st, kVTx);
                     const uint32_t dst = sbase + kVOff + st * kVStage;
                     for (int h = 0; h < 2; ++h)
-                        tma_load_4d_own(dst + h * 4 * kBox, &v_map, h ? y1 : y0, 2 * (int)rank,
+                        tma_load_v_own(dst + h * 4 * kBox, &v_map, h ? y1 : y0, 4 * (int)rank,
                                         mb + kBarVFull + 8 * st, pol);
                 }
                 gt += g.n_tiles;
@@ -615,7 +615,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                     const int idx = t + 128 * k, r = idx >> 3, c = idx & 7;
                     const float4 v =
                         *reinterpret_cast<const float4*>(stage + r * 128 + ((c ^ (r & 7)) << 4));
-                    const int col = (u >> 2) * 256 + (r >> 6) * 128 + (u & 3) * 32 + 4 * c;
+                    const int col = (r >> 6) * 256 + (u >> 2) * 128 + (u & 3) * 32 + 4 * c;
                     *reinterpret_cast<float4*>(ctx_base + (int64_t)(r & 63) * kValue + col) = v;
                 }
             }
@@ -697,12 +697,12 @@ cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWor
     const cuuint64_t row_bytes = tc::kLatent * 2;
     const cuuint64_t k_dims[3] = {64, rows, tc::kKBlocks}, k_str[2] = {row_bytes, 128};
     const cuuint32_t k_box[3] = {64, 32, tc::kKBlocks};
-    const cuuint64_t v_dims[4] = {64, rows, 4, 2}, v_str[3] = {row_bytes, 128, 512};
-    const cuuint32_t v_box[4] = {64, 32, 2, 2};
+    const cuuint64_t v_dims[3] = {64, rows, 8}, v_str[2] = {row_bytes, 128};
+    const cuuint32_t v_box[3] = {64, 32, 4};
     const cuuint64_t q_dims[3] = {64, static_cast<uint64_t>(a.batch) * tc::kHeads, tc::kKBlocks};
     const cuuint32_t q_box[3] = {64, tc::kHeadsPerCta, tc::kKBlocks};
     if (!tc::encode_f16(&k_map, a.cache, 3, k_dims, k_str, k_box) ||
-        !tc::encode_f16(&v_map, a.cache, 4, v_dims, v_str, v_box) ||
+        !tc::encode_f16(&v_map, a.cache, 3, v_dims, v_str, v_box) ||
         !tc::encode_f16(&q_map, ws.q16, 3, q_dims, k_str, q_box))
         return cudaErrorInvalidValue;
     const int64_t n4 = (int64_t)a.batch * tc::kHeads * tc::kLatent / 4;

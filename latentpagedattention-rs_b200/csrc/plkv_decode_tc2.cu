@@ -143,25 +143,25 @@ __device__ __forceinline__ void tma_k_pair(uint32_t dst, const CUtensorMap* map,
           "r"(cluster_bar), "l"(policy)
         : "memory");
 }
-// The four value blocks {z0, z0+1, z0+4, z0+5} of 32 rows (4-D view: 64
-// columns, rows, 4 blocks at 128 B, 2 groups at 512 B).  Pair form: completes
-// on the leader's barrier; own form: on a barrier of this CTA.
+// The four value blocks [z0, z0 + 4) of 32 rows (3-D view: 64 columns, rows,
+// 8 blocks at 128 B: one 512-byte run per row).  Pair form: completes on the
+// leader's barrier; own form: on a barrier of this CTA.
 __device__ __forceinline__ void tma_v_pair(uint32_t dst, const CUtensorMap* map, int y, int z0,
                                            uint32_t cluster_bar, uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z0), "r"(0),
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z0),
           "r"(cluster_bar), "l"(policy)
         : "memory");
 }
 __device__ __forceinline__ void tma_v_own(uint32_t dst, const CUtensorMap* map, int y, int z0,
                                           uint32_t bar, uint64_t policy) {
     asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z0), "r"(0),
-          "r"(bar), "l"(policy)
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y), "r"(z0), "r"(bar),
+          "l"(policy)
         : "memory");
 }
 // Q rows [y, y + 64) x all nine column blocks (3-D), pair form.
@@ -364,13 +364,13 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                         const uint32_t dst = sbase + kVOff + st * kVStage;
                         if (v != tail) {
                             if (leader) mbar_arrive_expect_tx(mb + kBarVFull + 8 * st, 2u * kVStage);
-                            tma_v_pair(dst, &v_map, y, 2 * (int)rank,
+                            tma_v_pair(dst, &v_map, y, 4 * (int)rank,
                                        mapa(mb + kBarVFull + 8 * st, 0), pol);
                         } else {
                             // Landed in this CTA alone: the softmax warps zero
                             // its rows past the end, then report to the leader.
                             mbar_arrive_expect_tx(mb + kBarVTail, kVStage);
-                            tma_v_own(dst, &v_map, y, 2 * (int)rank, mb + kBarVTail, pol);
+                            tma_v_own(dst, &v_map, y, 4 * (int)rank, mb + kBarVTail, pol);
                             if (leader) mbar_arrive_local(mb + kBarVFull + 8 * st);
                         }
                         ++vs;
@@ -652,7 +652,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                         *reinterpret_cast<const float4*>(stage + r * 128 + ((c ^ (r & 7)) << 4));
                     // thread r of the softmax group: lane t_r, column half ch_r
                     const int wr = r >> 5, t_r = 32 * (wr & 3) + (r & 31), ch_r = wr >> 2;
-                    const int col = 256 * ch_r + 128 * (t_r >> 6) + 32 * u + 4 * c;
+                    const int col = 256 * (t_r >> 6) + 128 * ch_r + 32 * u + 4 * c;
                     *reinterpret_cast<float4*>(ctx_base + (int64_t)(t_r & 63) * kValue + col) = v;
                 }
             }
@@ -696,12 +696,12 @@ cudaError_t launch_latent_partial_tc2(const plkv_latent_decode_args& a, DecodeWo
     const cuuint64_t row_bytes = tc2::kLatent * 2;
     const cuuint64_t k_dims[3] = {64, rows, tc2::kCb}, k_str[2] = {row_bytes, 128};
     const cuuint32_t k_box[3] = {64, tc2::kPage, tc2::kCbPerStage};
-    const cuuint64_t v_dims[4] = {64, rows, 4, 2}, v_str[3] = {row_bytes, 128, 512};
-    const cuuint32_t v_box[4] = {64, tc2::kVRows, 2, 2};
+    const cuuint64_t v_dims[3] = {64, rows, 8}, v_str[2] = {row_bytes, 128};
+    const cuuint32_t v_box[3] = {64, tc2::kVRows, 4};
     const cuuint64_t q_dims[3] = {64, static_cast<uint64_t>(a.batch) * tc2::kHeads, tc2::kCb};
     const cuuint32_t q_box[3] = {64, tc2::kHeadsPerCta, tc2::kCb};
     if (!tc::encode_f16_map(&k_map, a.cache, 3, k_dims, k_str, k_box) ||
-        !tc::encode_f16_map(&v_map, a.cache, 4, v_dims, v_str, v_box) ||
+        !tc::encode_f16_map(&v_map, a.cache, 3, v_dims, v_str, v_box) ||
         !tc::encode_f16_map(&q_map, ws.q16, 3, q_dims, k_str, q_box))
         return cudaErrorInvalidValue;
     const int64_t n4 = (int64_t)a.batch * tc2::kHeads * tc2::kLatent / 4;
