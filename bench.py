@@ -1203,6 +1203,13 @@ def run_kernel_suite(args) -> dict:
     timed("out_proj W_o (64 x 16384 x 7168, FP32)", ["out_proj_partial_kernel", "out_proj_reduce_kernel"],
           lambda: ops.out_proj(xo, w_o, out=oo), w_o.numel() * 4 + xo.numel() * 4 + oo.numel() * 4,
           "FP32 CUDA-core bound (15 GFLOP)")
+    wo_tc_ws = torch.empty(int(ops.lib().plkv_out_proj_tc_workspace_size(
+        64, 7168, ops.default_out_proj_tc_splits(16384, 7168, 64, dev))), dtype=torch.uint8,
+        device=dev)
+    timed("out_proj_tc W_o (64 x 16384 x 7168, TF32 tensor cores)",
+          ["out_proj_tf32_kernel", "out_proj_reduce_kernel"],
+          lambda: ops.out_proj_tc(xo, w_o, out=oo, workspace=wo_tc_ws),
+          w_o.numel() * 4 + xo.numel() * 4 + oo.numel() * 4)
     del w_o
     cs, ls = randn(8, 1024, 128), randn(8, 1024)
     timed("lse_merge (8 shards x 1024 rows x 128)", ["lse_merge_kernel"],

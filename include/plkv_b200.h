@@ -346,6 +346,19 @@ int plkv_out_proj(const float* x, const float* w_o, float* out, int32_t batch, i
                   int32_t out_dim, int32_t k_splits, void* workspace, size_t workspace_bytes,
                   plkv_stream_t stream);
 
+/* W_o output projection on the tensor cores: the same product with tcgen05
+ * kind::tf32 MMAs on the FP32 W_o as stored (both operands rounded to TF32,
+ * FP32 accumulation; about 1e-3 normwise relative error, against the FP32
+ * plkv_out_proj's 1e-6).  Extension, no counterpart in the reference.
+ * in_dim % 32 == 0, out_dim % 32 == 0, 1 <= k_splits <= in_dim / 32; x, w_o and
+ * the workspace 256-byte aligned; the workspace holds
+ * plkv_out_proj_tc_workspace_size(batch, out_dim, k_splits) bytes.  A wait
+ * that runs out of time raises PLKV_FLAG_TIMEOUT in *err_flags (may be NULL). */
+size_t plkv_out_proj_tc_workspace_size(int32_t batch, int32_t out_dim, int32_t k_splits);
+int plkv_out_proj_tc(const float* x, const float* w_o, float* out, int32_t batch, int32_t in_dim,
+                     int32_t out_dim, int32_t k_splits, void* workspace, size_t workspace_bytes,
+                     int32_t* err_flags, plkv_stream_t stream);
+
 /* ------------------------------------------------------ full-KV baseline */
 
 typedef struct plkv_fullkv_decode_args {

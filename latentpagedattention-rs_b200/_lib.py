@@ -102,6 +102,8 @@ SIGNATURES = {
     "plkv_lse_merge": (ctypes.c_int, [_P, _P, _I32, _I64, _I32, _P, _P, _P]),
     "plkv_out_proj_workspace_size": (_SZ, [_I32, _I32, _I32]),
     "plkv_out_proj": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _I32, _P, _SZ, _P]),
+    "plkv_out_proj_tc_workspace_size": (_SZ, [_I32, _I32, _I32]),
+    "plkv_out_proj_tc": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _I32, _P, _SZ, _P, _P]),
     "plkv_fullkv_decode_workspace_size": (_SZ, [_I32, _I32, _I32, _I32]),
     "plkv_fullkv_decode": (ctypes.c_int, [ctypes.POINTER(FullKVDecodeArgs), _P]),
     "plkv_selftest_bounded_wait": (ctypes.c_int, [_P, _P, _P, _P]),

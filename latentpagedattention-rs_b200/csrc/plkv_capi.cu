@@ -40,6 +40,8 @@ cudaError_t launch_lse_merge(const float*, const float*, int, int64_t, int, floa
                              cudaStream_t);
 cudaError_t launch_out_proj(const float*, const float*, float*, int, int, int, int, float*,
                             cudaStream_t);
+cudaError_t launch_out_proj_tf32(const float*, const float*, float*, int, int, int, int, float*,
+                                 int32_t*, int32_t*, cudaStream_t);
 }  // namespace plkv
 
 using namespace plkv;
@@ -372,6 +374,31 @@ int plkv_out_proj(const float* x, const float* w_o, float* out, int32_t batch, i
         return PLKV_ERR_WORKSPACE;
     return launch_out_proj(x, w_o, out, batch, in_dim, out_dim, k_splits,
                            static_cast<float*>(workspace), (cudaStream_t)stream) == cudaSuccess
+               ? PLKV_OK
+               : PLKV_ERR_CUDA;
+}
+
+size_t plkv_out_proj_tc_workspace_size(int32_t batch, int32_t out_dim, int32_t k_splits) {
+    if (batch <= 0 || out_dim <= 0 || k_splits <= 0) return 0;
+    return 256 + size_t(k_splits) * batch * out_dim * 4;
+}
+
+int plkv_out_proj_tc(const float* x, const float* w_o, float* out, int32_t batch, int32_t in_dim,
+                     int32_t out_dim, int32_t k_splits, void* workspace, size_t workspace_bytes,
+                     int32_t* err_flags, plkv_stream_t stream) {
+    if (batch <= 0 || in_dim <= 0 || out_dim <= 0 || k_splits <= 0) return PLKV_ERR_ZERO_VALUE;
+    if (!x || !w_o || !out || !workspace) return PLKV_ERR_INVALID_ARGUMENT;
+    if (in_dim % 32 || out_dim % 32 || k_splits > in_dim / 32 || batch > 65535 * 128)
+        return PLKV_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_o) |
+         reinterpret_cast<uintptr_t>(workspace)) & 255)
+        return PLKV_ERR_INVALID_ARGUMENT;
+    if (workspace_bytes < plkv_out_proj_tc_workspace_size(batch, out_dim, k_splits))
+        return PLKV_ERR_WORKSPACE;
+    int32_t* ctl = static_cast<int32_t*>(workspace);
+    float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+    return launch_out_proj_tf32(x, w_o, out, batch, in_dim, out_dim, k_splits, partial, ctl,
+                                err_flags, (cudaStream_t)stream) == cudaSuccess
                ? PLKV_OK
                : PLKV_ERR_CUDA;
 }

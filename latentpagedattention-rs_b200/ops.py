@@ -515,6 +515,39 @@ def out_proj(x: torch.Tensor, w_o: torch.Tensor, *, out: torch.Tensor | None = N
     return out
 
 
+def default_out_proj_tc_splits(in_dim: int, out_dim: int, batch: int,
+                               device: torch.device | None = None) -> int:
+    """K splits of the tensor-core W_o product: enough CTAs (256 output
+    columns x 128 batch rows x a K range each) to cover every SM once."""
+    sms = default_target_items(device) // 2
+    tiles = ((out_dim + 255) // 256) * ((batch + 127) // 128)
+    return max(1, min(in_dim // 32, sms // max(tiles, 1)))
+
+
+def out_proj_tc(x: torch.Tensor, w_o: torch.Tensor, *, out: torch.Tensor | None = None,
+                k_splits: int | None = None, workspace: torch.Tensor | None = None,
+                flags: torch.Tensor | None = None) -> torch.Tensor:
+    """W_o output projection ``out = x @ w_o`` on the tensor cores (TF32
+    operands, FP32 accumulation; ~1e-3 normwise relative error)."""
+    _need_cuda("x", x, torch.float32)
+    _need_cuda("w_o", w_o, torch.float32)
+    B, K = x.shape
+    K2, N = w_o.shape
+    if K2 != K:
+        raise ValueError("W_o rows must equal the concatenated head width")
+    if k_splits is None:
+        k_splits = default_out_proj_tc_splits(K, N, B, x.device)
+    if out is None:
+        out = torch.empty((B, N), dtype=torch.float32, device=x.device)
+    need = int(lib().plkv_out_proj_tc_workspace_size(B, N, k_splits))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    check(lib().plkv_out_proj_tc(_ptr(x), _ptr(w_o), _ptr(out), B, K, N, k_splits,
+                                 _ptr(workspace), workspace.numel(), _ptr(flags),
+                                 _stream(x.device)), "plkv_out_proj_tc")
+    return out
+
+
 # ------------------------------------------------- materialised reconstruction
 
 def reconstruct_kv(latent: torch.Tensor, w_k: torch.Tensor, w_v: torch.Tensor, *,

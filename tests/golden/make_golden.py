@@ -2,7 +2,7 @@
 
 Run in a checkout that has tatavishnurao/LatentPagedAttention-rs next to it:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 It imports ``python_ref/latent_paged_attention`` and writes
 
@@ -211,7 +211,9 @@ def model_shaped(ar, cr, wl) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("PLKV_REFERENCE"), required=
+                    os.environ.get("PLKV_REFERENCE") is None,
+                    help="root of a checkout of the reference project (or set PLKV_REFERENCE)")
     args = ap.parse_args()
     ar, cr, fx = _load_reference(args.reference)
     wl = _load_workloads()

@@ -151,3 +151,25 @@ def test_materialised_decode_matches_oracle_and_direct_path():
     direct = ops.latent_decode(q_lat, torch.as_tensor(c["cache"], device=DEV), tables, lens,
                                plan, scale=scale, value_dim=L, w_v=_hm(c["w_v"], KV, D))
     assert rel_err(ctx, direct["ctx"].cpu().numpy()) <= 2e-2
+
+
+@pytest.mark.parametrize("B,K,N", [(64, 16384, 7168), (1, 4096, 4096), (2, 64, 64), (200, 512, 320)])
+def test_out_proj_tensor_cores_vs_oracle(B, K, N):
+    """W_o on the tensor cores (TF32 operands, FP32 accumulation) against the
+    FP64 oracle at 2e-3 normwise, and against the FP32 CUDA-core product."""
+    ops = _ops()
+    rng = np.random.default_rng(B + N)
+    x = rng.standard_normal((B, K), dtype=np.float32)
+    w = (rng.standard_normal((K, N), dtype=np.float32) / np.float32(math.sqrt(K)))
+    xt, wt = torch.as_tensor(x, device=DEV), torch.as_tensor(w, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    got = ops.out_proj_tc(xt, wt, flags=flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
+    g = got.cpu().numpy()
+    rows = np.unique(np.array([0, B // 2, B - 1]))
+    exp = c_ref.out_proj(x[rows], w, acc64=True)
+    assert rel_err(g[rows], exp) <= 2e-3
+    if B <= 64:
+        ref32 = ops.out_proj(xt, wt).cpu().numpy()
+        assert rel_err(g, ref32) <= 2e-3

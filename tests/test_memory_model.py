@@ -40,10 +40,13 @@ def test_cli_table_and_report():
     assert r["latent_bytes"] == 1048576 * 1152
 
 
-_REF = "/root/reference/python_ref"
+# The reference's python_ref directory, when a checkout is available (set
+# PLKV_REFERENCE to the reference project's root).
+_REF = os.path.join(os.environ.get("PLKV_REFERENCE", ""), "python_ref")
 
 
-@pytest.mark.skipif(not os.path.isdir(_REF), reason="reference sources not present")
+@pytest.mark.skipif(not os.environ.get("PLKV_REFERENCE") or not os.path.isdir(_REF),
+                    reason="PLKV_REFERENCE does not name a reference checkout")
 def test_matches_reference_module():
     sys.path.insert(0, _REF)
     try:
