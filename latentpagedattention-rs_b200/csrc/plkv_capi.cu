@@ -313,7 +313,7 @@ int plkv_latent_decode_partial(const plkv_latent_decode_args* a, plkv_stream_t s
                                          a->latent_dim, a->value_dim);
     cudaError_t e;
     if (a->mode == PLKV_MODE_TC_F16) {
-        static const bool v1 = getenv("PLKV_TC_V1") != nullptr;  // A/B against the old pass
+        static const bool v1 = getenv("PLKV_TC_V2") == nullptr;  // A/B of the two passes
         if (v1) {
             if (!tc_supported(*a)) return PLKV_ERR_UNSUPPORTED;
             e = launch_latent_partial_tc(*a, ws, (cudaStream_t)stream);
