@@ -567,12 +567,21 @@ def run_ours(args, s, rank: int, world: int):
                                  device=dev))
         wo_splits = wo_ws = None
         if w_o is not None:
-            wo_splits = ops.default_out_proj_splits(w_o.shape[0], w_o.shape[1], dev)
-            wo_ws = torch.empty(max(1, ops.out_proj_workspace_bytes(out.shape[0], w_o.shape[1],
-                                                                    wo_splits)),
-                                dtype=torch.uint8, device=dev)
+            if mode == "tc":
+                # tensor-core mode: W_o on the tensor cores (TF32 operands)
+                wo_splits = ops.default_out_proj_tc_splits(w_o.shape[0], w_o.shape[1],
+                                                           out.shape[0], dev)
+                wo_ws = torch.empty(int(ops.lib().plkv_out_proj_tc_workspace_size(
+                    out.shape[0], w_o.shape[1], wo_splits)), dtype=torch.uint8, device=dev)
+            else:
+                wo_splits = ops.default_out_proj_splits(w_o.shape[0], w_o.shape[1], dev)
+                wo_ws = torch.empty(max(1, ops.out_proj_workspace_bytes(
+                    out.shape[0], w_o.shape[1], wo_splits)), dtype=torch.uint8, device=dev)
 
         def project(a, w):
+            if mode == "tc":
+                return ops.out_proj_tc(a, w, out=out, k_splits=wo_splits, workspace=wo_ws,
+                                       flags=flags)
             return ops.out_proj(a, w, out=out, k_splits=wo_splits, workspace=wo_ws)
 
         def step(q_src, rows_src, ev=None):

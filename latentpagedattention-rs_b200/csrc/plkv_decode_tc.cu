@@ -679,11 +679,12 @@ bool encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64
 }
 
 bool encode_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank,
-                const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box) {
+                const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                CUtensorMapSwizzle swizzle) {
     if (!load_encode()) return false;
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     return g_encode(map, type, rank, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

@@ -78,18 +78,24 @@ constexpr int kKStagesPerTile = kCb / kCbPerStage;            // 3
 constexpr uint32_t kAtom = 64 * 128;                          // 64 rows x 64 FP16 (8 KiB)
 constexpr uint32_t kQBytes = kCb * kAtom;                     // 72 KiB
 constexpr uint32_t kKStage = kCbPerStage * kAtom;             // 24 KiB
-constexpr int kNK = 3;
+#ifndef PLKV_TC2_NK
+#define PLKV_TC2_NK 3
+#endif
+#ifndef PLKV_TC2_NV
+#define PLKV_TC2_NV 3
+#endif
+constexpr int kNK = PLKV_TC2_NK;                              // K ring stages (24 KiB)
 constexpr int kVRows = 32;
 constexpr uint32_t kVBox = kVRows * 128;                      // 4 KiB: 32 rows x 64 FP16
 constexpr uint32_t kVStage = 4 * kVBox;                       // 16 KiB
-constexpr int kNV = 2;
+constexpr int kNV = PLKV_TC2_NV;                              // V ring stages (16 KiB)
 constexpr uint32_t kPBytes = 2 * kAtom;                       // 16 KiB: 64 heads x 128 tokens
 constexpr uint32_t kQOff = 0;
 constexpr uint32_t kKOff = kQOff + kQBytes;
 constexpr uint32_t kVOff = kKOff + kNK * kKStage;
 constexpr uint32_t kPOff = kVOff + kNV * kVStage;
 constexpr uint32_t kMiscOff = kPOff + 2 * kPBytes;
-constexpr uint32_t kMiscBytes = 4096;
+constexpr uint32_t kMiscBytes = 2048;
 constexpr uint32_t kSmemBytes = kMiscOff + kMiscBytes;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 0;                                // O half i at 128 i
@@ -113,11 +119,11 @@ enum : uint32_t {
     kBarODone = kBarPFull + 16,           // [2] both: O of the tile completed
     kTmemSlot = kBarODone + 16,
     kAbort = kTmemSlot + 4,
-    kRedMax = 256,              // [2][4][64] float
-    kRedSum = kRedMax + 2048,   // [4][64] float
+    kRedMax = 512,              // [4][64] float: tile max (softmax) / row sum (epilogue)
+    kRedSum = kRedMax,
 };
 static_assert(kAbort + 4 <= kRedMax, "barriers");
-static_assert(kRedSum + 1024 <= kMiscBytes, "misc region");
+static_assert(kRedMax + 1024 <= kMiscBytes, "misc region");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ void named_sync_softmax() {
@@ -317,13 +323,21 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                 // for every S MMA of the previous item, so it follows them.
                 const int pre = min(kNK, kKStagesPerTile * g.n_tiles);
                 int sidx = 0;  // stage index within the item
+                // This CTA's page row of tile j, looked up one tile ahead so
+                // that the table read overlaps the waits for free stages.
+                auto page_row = [&](int j) -> int {
+                    return (j < g.n_tiles && kPage * (int)rank < tile_valid(g, j))
+                               ? pool_row(g.seq, g.t_begin + kTile * j + kPage * (int)rank, tables,
+                                          max_blocks, num_physical, bs, flags)
+                               : 0;
+                };
+                int y_next = page_row(0);
                 for (int j = 0; ok && j < g.n_tiles; ++j) {
                     const int vc = tile_valid(g, j);
                     const bool mine = kPage * (int)rank < vc;      // this CTA's page exists
                     const bool both = kPage < vc;
-                    const int y = mine ? pool_row(g.seq, g.t_begin + kTile * j + kPage * (int)rank,
-                                                  tables, max_blocks, num_physical, bs, flags)
-                                       : 0;
+                    const int y = y_next;
+                    y_next = page_row(j + 1);
                     for (int c = 0; c < kKStagesPerTile; ++c, ++sidx) {
                         if (sidx == pre && !(ok = load_q())) break;
                         const int st = ks % kNK;
@@ -351,16 +365,27 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
             bool ok = true;
             for (int ii = i_begin; ok && ii < i_end; ++ii) {
                 const ItemGeom g = item_geom(items, ii, seq_lens, bs, cap, flags, false);
+                // Rows of the tile's two pages, looked up one tile ahead.
+                auto page_rows = [&](int j, int* r) {
+                    for (int h = 0; h < 2; ++h)
+                        r[h] = (j < g.n_tiles && kPage * h < tile_valid(g, j))
+                                   ? pool_row(g.seq, g.t_begin + kTile * j + kPage * h, tables,
+                                              max_blocks, num_physical, bs, flags)
+                                   : 0;
+                };
+                int nxt[2];
+                page_rows(0, nxt);
                 for (int j = 0; ok && j < g.n_tiles; ++j) {
                     const int vc = tile_valid(g, j);
                     const int tail = tail_stage(g, j);
+                    const int pr0 = nxt[0], pr1 = nxt[1];
+                    page_rows(j + 1, nxt);
                     for (int v = 0; v * kVRows < vc; ++v) {
                         const int st = vs % kNV;
                         if (vs >= kNV &&
                             !(ok = mbar_wait(mb + kBarVEmpty + 8 * st, ((vs / kNV) - 1) & 1, wc)))
                             break;
-                        const int y = pool_row(g.seq, g.t_begin + kTile * j + kVRows * v, tables,
-                                               max_blocks, num_physical, bs, flags);
+                        const int y = (v < 2 ? pr0 : pr1) + kVRows * (v & 1);
                         const uint32_t dst = sbase + kVOff + st * kVStage;
                         if (v != tail) {
                             if (leader) mbar_arrive_expect_tx(mb + kBarVFull + 8 * st, 2u * kVStage);
@@ -383,90 +408,142 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
         // ---------------------------------------------- MMA issue (leader)
         // Issuer p: the S partial over column blocks cb = p, p + 2, ... of
         // every tile (p = 0: blocks 0, 2, 4, 6, 8; p = 1: 1, 3, 5, 7), and O
-        // half p.  Order per tile g: S(g), then O(g - 1), so that S of the next
-        // tile runs on the tensor pipe while the softmax of this one does.
+        // half p.  Each issuer schedules without blocking: the next K stage of
+        // S as soon as it landed (its tile's S buffer free, its item's Q
+        // loaded), and the next V stage of O as soon as it landed and the
+        // tile's P is ready, so that S of later tiles stays queued on the
+        // tensor pipe while the softmax of earlier ones runs.  Barriers are
+        // polled with test_wait, which never suspends the thread.
         if (leader && lane == 0) {
             const int p = warp == 1 ? 0 : 1;
             const uint32_t id_s = idesc_f16(128, kTile, false, false);
             const uint32_t id_o = idesc_f16(128, 256, false, true);
-            int ks = 0, vs = 0, tails = 0;
-            int g = 0;
-            bool ok = true;
-            // O of tile gt (item ii, tile j in it): half p over its valid
-            // 16-token steps.
-            auto issue_o = [&](int gt, int ii, int j) -> bool {
-                const ItemGeom go = item_geom(items, ii, seq_lens, bs, cap, flags, false);
-                const int ni = ii - i_begin;
-                const int pb = gt & 1;
-                if (!mbar_wait(mb + kBarPFull + 8 * pb, (gt >> 1) & 1, wc)) return false;
-                if (j == 0 && ni >= 1 && !mbar_wait(mb + kBarOFree, (ni - 1) & 1, wc)) return false;
-                tc_fence_after();
-                const int vc = tile_valid(go, j);
-                const int tail = tail_stage(go, j);
-                const int ksteps = (vc + 15) / 16;
-                const uint32_t preg = sbase + kPOff + pb * kPBytes;
-                for (int v = 0; v * kVRows < vc; ++v) {
-                    const int st = vs % kNV;
-                    if (!mbar_wait(mb + kBarVFull + 8 * st, (vs / kNV) & 1, wc)) return false;
-                    if (v == tail && !mbar_wait(mb + kBarVReady, tails & 1, wc)) return false;
-                    tc_fence_after();
-                    const uint32_t vreg = sbase + kVOff + st * kVStage + p * 2 * kVBox;
-                    for (int kk = 2 * v; kk < min(2 * v + 2, ksteps); ++kk) {
-                        const uint64_t a = sdesc_sw128(preg + (kk >> 2) * kAtom + (kk & 3) * 32, 16,
-                                                       1024);
-                        const uint64_t b = sdesc_sw128(vreg + (kk & 1) * 2048, kVBox, 1024);
-                        mma_pair_f16(tmem + kTmemO + 128 * p, a, b, id_o,
-                                     (j > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    mma_commit_pair(mb + kBarVEmpty + 8 * st, 0x3);
-                    if (v == tail) ++tails;
-                    ++vs;
-                }
-                mma_commit_pair(mb + kBarODone + 8 * pb, 0x3);
-                return true;
-            };
-            int prev_ii = -1, prev_j = -1;
-            int nq = 0;  // Q loads waited for (items with tokens)
-            for (int ii = i_begin; ok && ii < i_end; ++ii) {
-                const ItemGeom gs = item_geom(items, ii, seq_lens, bs, cap, flags, false);
-                if (gs.n_tiles == 0) continue;
-                if (!(ok = mbar_wait(mb + kBarQFull, nq & 1, wc))) break;
-                ++nq;
-                for (int j = 0; ok && j < gs.n_tiles; ++j, ++g) {
-                    const int sb = g & 1;
-                    if (g >= 2 && !(ok = mbar_wait(mb + kBarSFree + 8 * sb, ((g - 2) >> 1) & 1, wc)))
-                        break;
-                    tc_fence_after();
-                    bool first = true;
-                    for (int c = 0; ok && c < kKStagesPerTile; ++c) {
+            // S cursor
+            int si = i_begin, sj = 0, sc = 0, sg = 0, ks = 0, nq = 0;
+            bool s_q = false, s_free = false;
+            ItemGeom gs = si < i_end ? item_geom(items, si, seq_lens, bs, cap, flags, false)
+                                     : ItemGeom{0, 0, 0, 0};
+            // O cursor
+            int oi = i_begin, oj = 0, ov = 0, og = 0, vs = 0, tails = 0;
+            bool o_p = false;
+            ItemGeom go = gs;
+            uint64_t idle_since = 0, next_check = 0;
+            while (si < i_end || oi < i_end) {
+                bool did = false;
+                if (si < i_end) {
+                    if (sj >= gs.n_tiles) {  // next item (its Q, if it has tokens)
+                        if (++si < i_end) gs = item_geom(items, si, seq_lens, bs, cap, flags, false);
+                        sj = 0;
+                        s_q = false;
+                        did = true;
+                    } else {
+                        if (!s_q && mbar_test_wait(mb + kBarQFull, nq & 1)) s_q = true;
+                        if (s_q && !s_free &&
+                            (sg < 2 || mbar_test_wait(mb + kBarSFree + 8 * (sg & 1),
+                                                      ((sg - 2) >> 1) & 1)))
+                            s_free = true;
                         const int st = ks % kNK;
-                        if (!(ok = mbar_wait(mb + kBarKFull + 8 * st, (ks / kNK) & 1, wc))) break;
-                        tc_fence_after();
-                        const uint32_t kreg = sbase + kKOff + st * kKStage;
-                        for (int cc = 0; cc < kCbPerStage; ++cc) {
-                            const int cb = kCbPerStage * c + cc;
-                            if ((cb & 1) != p) continue;
+                        if (s_q && s_free && mbar_test_wait(mb + kBarKFull + 8 * st, (ks / kNK) & 1)) {
+                            tc_fence_after();
+                            const int sb = sg & 1;
+                            const uint32_t kreg = sbase + kKOff + st * kKStage;
+                            for (int cc = 0; cc < kCbPerStage; ++cc) {
+                                const int cb = kCbPerStage * sc + cc;
+                                if ((cb & 1) != p) continue;
 #pragma unroll
-                            for (int kq = 0; kq < 4; ++kq) {
-                                const uint64_t a =
-                                    sdesc_sw128(sbase + kQOff + cb * kAtom + kq * 32, 16, 1024);
-                                const uint64_t b = sdesc_sw128(kreg + cc * kAtom + kq * 32, 16, 1024);
-                                mma_pair_f16(tmem + s_col(p, sb), a, b, id_s, first ? 0u : 1u);
-                                first = false;
+                                for (int kq = 0; kq < 4; ++kq) {
+                                    const uint64_t a =
+                                        sdesc_sw128(sbase + kQOff + cb * kAtom + kq * 32, 16, 1024);
+                                    const uint64_t b =
+                                        sdesc_sw128(kreg + cc * kAtom + kq * 32, 16, 1024);
+                                    mma_pair_f16(tmem + s_col(p, sb), a, b, id_s,
+                                                 (cb == p && kq == 0) ? 0u : 1u);
+                                }
                             }
+                            mma_commit_pair(mb + kBarKEmpty + 8 * st, 0x3);
+                            ++ks;
+                            if (++sc == kKStagesPerTile) {
+                                mma_commit_pair(mb + kBarSFull + 8 * sb, 0x3);
+                                if (sj == gs.n_tiles - 1) {
+                                    mma_commit_pair(mb + kBarQFree, 0x3);
+                                    ++nq;
+                                }
+                                sc = 0;
+                                ++sj;
+                                ++sg;
+                                s_free = false;
+                            }
+                            did = true;
                         }
-                        mma_commit_pair(mb + kBarKEmpty + 8 * st, 0x3);
-                        ++ks;
                     }
-                    if (!ok) break;
-                    mma_commit_pair(mb + kBarSFull + 8 * sb, 0x3);
-                    if (j == gs.n_tiles - 1) mma_commit_pair(mb + kBarQFree, 0x3);
-                    if (prev_ii >= 0 && !(ok = issue_o(g - 1, prev_ii, prev_j))) break;
-                    prev_ii = ii;
-                    prev_j = j;
+                }
+                if (oi < i_end && (oi < si || (oi == si && oj < sj))) {
+                    // O of tile og (item oi, tile oj) once its S was issued
+                    if (oj >= go.n_tiles) {
+                        if (++oi < i_end) go = item_geom(items, oi, seq_lens, bs, cap, flags, false);
+                        oj = 0;
+                        did = true;
+                    } else {
+                        const int pb = og & 1;
+                        if (!o_p && mbar_test_wait(mb + kBarPFull + 8 * pb, (og >> 1) & 1) &&
+                            (oj > 0 || oi == i_begin ||
+                             mbar_test_wait(mb + kBarOFree, (oi - i_begin - 1) & 1)))
+                            o_p = true;
+                        const int vc = tile_valid(go, oj);
+                        const int tail = tail_stage(go, oj);
+                        const int st = vs % kNV;
+                        if (o_p && mbar_test_wait(mb + kBarVFull + 8 * st, (vs / kNV) & 1) &&
+                            (ov != tail || mbar_test_wait(mb + kBarVReady, tails & 1))) {
+                            tc_fence_after();
+                            const int ksteps = (vc + 15) / 16;
+                            const uint32_t preg = sbase + kPOff + pb * kPBytes;
+                            const uint32_t vreg = sbase + kVOff + st * kVStage + p * 2 * kVBox;
+                            for (int kk = 2 * ov; kk < min(2 * ov + 2, ksteps); ++kk) {
+                                const uint64_t a = sdesc_sw128(
+                                    preg + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
+                                const uint64_t b = sdesc_sw128(vreg + (kk & 1) * 2048, kVBox, 1024);
+                                mma_pair_f16(tmem + kTmemO + 128 * p, a, b, id_o,
+                                             (oj > 0 || kk > 0) ? 1u : 0u);
+                            }
+                            mma_commit_pair(mb + kBarVEmpty + 8 * st, 0x3);
+                            if (ov == tail) ++tails;
+                            ++vs;
+                            if (++ov * kVRows >= vc) {
+                                mma_commit_pair(mb + kBarODone + 8 * pb, 0x3);
+                                ov = 0;
+                                ++oj;
+                                ++og;
+                                o_p = false;
+                            }
+                            did = true;
+                        }
+                    }
+                }
+                // Idle: the abort flag (shared memory) is checked on every
+                // pass, the launch's abort word and the time limit only every
+                // kFlagPollNs, so that polling stays a shared-memory loop.
+                if (did) {
+                    idle_since = 0;
+                } else if (*abort_flag) {
+                    break;
+                } else {
+                    const uint64_t now = globaltimer();
+                    if (idle_since == 0) {
+                        idle_since = now;
+                        next_check = now + kFlagPollNs;
+                    } else if (now >= next_check) {
+                        next_check = now + kFlagPollNs;
+                        if (*wc.abort) {
+                            *abort_flag = 1;
+                            break;
+                        }
+                        if (now - idle_since > kWaitLimitNs) {
+                            wait_give_up(wc);
+                            break;
+                        }
+                    }
                 }
             }
-            if (ok && prev_ii >= 0) ok = issue_o(g - 1, prev_ii, prev_j);
         }
         __syncwarp();
     } else if (warp >= 4) {
@@ -478,8 +555,8 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
         const int hl = t & 63, th = t >> 6;       // head in the CTA, token / value half
         const int red = th * 2 + ch;              // the head's four threads
         const uint32_t lane_base = static_cast<uint32_t>(32 * wq) << 16;
-        const uint32_t sfree_leader[2] = {mapa(mb + kBarSFree, 0), mapa(mb + kBarSFree + 8, 0)};
-        const uint32_t pfull_leader[2] = {mapa(mb + kBarPFull, 0), mapa(mb + kBarPFull + 8, 0)};
+        const uint32_t sfree_leader0 = mapa(mb + kBarSFree, 0), sfree_leader1 = mapa(mb + kBarSFree + 8, 0);
+        const uint32_t pfull_leader0 = mapa(mb + kBarPFull, 0), pfull_leader1 = mapa(mb + kBarPFull + 8, 0);
         const uint32_t ofree_leader = mapa(mb + kBarOFree, 0);
         const uint32_t vready_leader = mapa(mb + kBarVReady, 0);
         bool ok = true;
@@ -516,12 +593,14 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                     if (tok0 + i >= vc) s[i] = -INFINITY;
                     mx = fmaxf(mx, s[i]);
                 }
-                red_max[(b * 4 + red) * 64 + hl] = mx;
+                // One buffer suffices: the next tile's writes follow the
+                // named barrier before P is published, after every read below.
+                red_max[red * 64 + hl] = mx;
                 named_sync_softmax();
-                if (ok && ts == 0) mbar_arrive_cluster(sfree_leader[b]);
-                float mt = red_max[(b * 4) * 64 + hl];
+                if (ok && ts == 0) mbar_arrive_cluster(b ? sfree_leader1 : sfree_leader0);
+                float mt = red_max[hl];
 #pragma unroll
-                for (int k = 1; k < 4; ++k) mt = fmaxf(mt, red_max[(b * 4 + k) * 64 + hl]);
+                for (int k = 1; k < 4; ++k) mt = fmaxf(mt, red_max[k * 64 + hl]);
                 const float m_new = fmaxf(m_use, mt);
                 const bool resc = m_new > m_use + kTau;
                 float alpha = 1.f;
@@ -578,7 +657,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                 fence_proxy_async_smem();
                 tc_fence_before();
                 named_sync_softmax();
-                if (ok && ts == 0) mbar_arrive_cluster(pfull_leader[b]);
+                if (ok && ts == 0) mbar_arrive_cluster(b ? pfull_leader1 : pfull_leader0);
                 // V stages of this tile (the producer's and issuers' count).
                 const int tail = tail_stage(gi, j);
                 const int nvs = (vc + kVRows - 1) / kVRows;

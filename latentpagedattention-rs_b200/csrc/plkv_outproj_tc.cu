@@ -13,9 +13,11 @@
 // of the K splits go to the workspace and are added in a fixed order by the
 // reduction kernel of plkv_combine.cu.
 //
-// Operands in shared memory, SWIZZLE_128B: x is K-major (A: 128 rows x 32
-// FP32 per stage); W_o is MN-major (B: 8 blocks of 32 columns x 32 rows; LBO =
-// 4 KiB between column blocks, SBO = 1 KiB between 8-row groups).  Warp 0
+// Operands in shared memory: x is K-major with the 128-byte swizzle (A: 128
+// rows x 32 FP32 per stage); W_o is MN-major, for which 32-bit operands take
+// the 128-byte swizzle of 32-byte atoms (B: 8 blocks of 32 columns x 32 rows,
+// 32-byte chunks permuted across 4-row groups; LBO = 4 KiB between column
+// blocks, SBO = 512 B between 4-row groups; descriptor layout type 1).  Warp 0
 // loads, warp 1 allocates tensor memory and issues, warps 2..5 read the
 // accumulator (each its TMEM lane quarter) and store the partial sums.  Every
 // wait is bounded (1 s, PLKV_FLAG_TIMEOUT).
@@ -46,6 +48,14 @@ enum : uint32_t { kBarFull = 0, kBarEmpty = 8 * kStages, kBarDone = 16 * kStages
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 16) |
                             (static_cast<uint32_t>(kN >> 3) << 17) |
                             (static_cast<uint32_t>(kM >> 4) << 24);
+
+// Shared-memory descriptor of an MN-major operand of 32-bit elements with the
+// 128-byte swizzle of 32-byte atoms (layout type 1), version 1.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128_32b(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (1ull << 61);
+}
 
 __device__ __forceinline__ void tmem_alloc1(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -157,7 +167,7 @@ out_proj_tf32_kernel(const __grid_constant__ CUtensorMap w_map,
 #pragma unroll
                 for (int kq = 0; kq < kKc / 8; ++kq) {
                     const uint64_t a = sdesc_sw128(xst + kq * 32, 16, 1024);
-                    const uint64_t b = sdesc_sw128(wst + kq * 1024, kKc * 128, 1024);
+                    const uint64_t b = sdesc_mn_sw128_32b(wst + kq * 1024, kKc * 128, 512);
                     mma_tf32(tmem, a, b, kIdesc, (i > 0 || kq > 0) ? 1u : 0u);
                 }
                 mma_commit1(mb + kBarEmpty + 8 * s);
@@ -206,7 +216,8 @@ out_proj_tf32_kernel(const __grid_constant__ CUtensorMap w_map,
 
 namespace tc {
 bool encode_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank,
-                const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box);
+                const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                CUtensorMapSwizzle swizzle);
 }
 __global__ void out_proj_reduce_kernel(const float* __restrict__ partial, float* __restrict__ out,
                                        int S, int64_t BN);
@@ -221,8 +232,10 @@ cudaError_t launch_out_proj_tf32(const float* x, const float* w, float* out, int
     const cuuint64_t x_dims[2] = {(cuuint64_t)K, (cuuint64_t)B};
     const cuuint64_t x_str[1] = {(cuuint64_t)K * 4};
     const cuuint32_t x_box[2] = {wo::kKc, wo::kM};
-    if (!tc::encode_map(&w_map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, w, 3, w_dims, w_str, w_box) ||
-        !tc::encode_map(&x_map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, x, 2, x_dims, x_str, x_box))
+    if (!tc::encode_map(&w_map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, w, 3, w_dims, w_str, w_box,
+                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+        !tc::encode_map(&x_map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, x, 2, x_dims, x_str, x_box,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaMemsetAsync(ctl, 0, 4, st);
     if (e != cudaSuccess) return e;

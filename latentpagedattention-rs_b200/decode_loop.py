@@ -94,7 +94,13 @@ class PagedLatentDecodeLoop:
         self.workspace = torch.empty(
             ops.latent_workspace_bytes(self.plan.n_items, B, q_heads, L, Lv), dtype=torch.uint8,
             device=dev)
-        if w_o is not None:
+        if w_o is not None and mode == "tc":
+            # tensor-core mode: W_o on the tensor cores too (TF32 operands)
+            self.wo_splits = ops.default_out_proj_tc_splits(w_o.shape[0], w_o.shape[1], B, dev)
+            self.wo_workspace = torch.empty(
+                int(ops.lib().plkv_out_proj_tc_workspace_size(B, w_o.shape[1], self.wo_splits)),
+                dtype=torch.uint8, device=dev)
+        elif w_o is not None:
             self.wo_splits = ops.default_out_proj_splits(w_o.shape[0], w_o.shape[1], dev)
             self.wo_workspace = torch.empty(
                 max(1, ops.out_proj_workspace_bytes(B, w_o.shape[1], self.wo_splits)),
@@ -123,7 +129,11 @@ class PagedLatentDecodeLoop:
             ev[1].record()
         ops.latent_decode(q_lat, self.cache, self.tables, self.seq_lens, self.plan,
                           phase="combine", **kw)
-        if self.w_o is not None:
+        if self.w_o is not None and self.mode == "tc":
+            ops.out_proj_tc(self.ctx[i].reshape(self.ctx.shape[1], -1), self.w_o,
+                            out=self.out[i], k_splits=self.wo_splits,
+                            workspace=self.wo_workspace, flags=self.flags)
+        elif self.w_o is not None:
             ops.out_proj(self.ctx[i].reshape(self.ctx.shape[1], -1), self.w_o, out=self.out[i],
                          k_splits=self.wo_splits, workspace=self.wo_workspace)
 
