@@ -798,6 +798,6 @@ def paged_gqa_decode_attention_intermediates(q, k_blocks, v_blocks, block_table,
 def tc_available(spec) -> bool:
     """Whether the tcgen05 decode kernel covers this workload's shapes
     (absorbed MLA: 128 query heads, latent 576 = 512 value + 64 RoPE,
-    block size a multiple of 64)."""
+    block size a multiple of 32)."""
     return (spec.q_heads == 128 and spec.latent_dim == 576 and spec.value_dim == 512
-            and spec.block_size % 64 == 0)
+            and spec.block_size % 32 == 0)

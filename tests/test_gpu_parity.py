@@ -389,13 +389,14 @@ def test_tensor_core_matches_exact_mode(ops, pkg, workers):
     assert rel_err(lt[fin], le[fin]) <= TC_REL
 
 
-@pytest.mark.parametrize("workers,bs", [(0, 64), (3, 64), (3, 256), (5, 128)])
+@pytest.mark.parametrize("workers,bs", [(0, 64), (3, 64), (3, 256), (5, 128), (4, 32)])
 def test_tensor_core_ignores_nonfinite_slots_past_the_end(ops, pkg, workers, bs):
     """Pool slots past a sequence's length (the rest of its last block, and
     blocks no table names) hold NaN and Inf: the tensor-core pass reads whole
     row groups there but must weigh them by exactly zero, as the exact pass,
-    which never reads them, does.  Block sizes 64 / 128 / 256 place a tile's
-    pages at every offset inside a block."""
+    which never reads them, does.  Block sizes 32 / 64 / 128 / 256 place a
+    tile's pages at every offset inside a block (32: a 64-token tile spans
+    two blocks)."""
     lens = [777, 131, 4101, 64, 33, 320]
     m = _mla_case(pkg, len(lens), lens, seed=17, bs=bs)
     cache = m["cache"].reshape(-1, m["L"])          # [P * bs, L] view
@@ -418,9 +419,9 @@ def test_tensor_core_ignores_nonfinite_slots_past_the_end(ops, pkg, workers, bs)
     assert rel_err(outs["tc"]["lse"].cpu(), outs["exact"]["lse"].cpu()) <= TC_REL
 
 
-def test_tensor_core_rejects_block_size_32(ops, pkg):
-    """The tensor-core pass loads one 64-row block per CTA and tile."""
-    m = _mla_case(pkg, 1, [100], seed=3, bs=32)
+def test_tensor_core_rejects_block_size_16(ops, pkg):
+    """The tensor-core pass loads whole 32-row halves of a block per TMA box."""
+    m = _mla_case(pkg, 1, [100], seed=3, bs=16)
     plan = ops.plan_workers(m["lens"], m["bs"])
     with pytest.raises(Exception, match="unsupported"):
         ops.latent_decode(t(m["q_lat"]), t(m["cache"]), t(m["tables"]), t(m["lens"]), plan,

@@ -222,3 +222,81 @@ def test_head_sharded_merge_equals_unsplit_decode(world, mode):
         tol = 2e-3 if mode == "tc" else 1e-5
         assert rel_err(got, full["ctx"].cpu()) <= tol
         assert rel_err(got_lse, full["lse"].cpu()) <= tol
+
+
+def _shard_worker(rank, world, port, out_path, mode):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import datetime
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    ops = importlib.import_module(PACKAGE + ".ops")
+    mg = importlib.import_module(PACKAGE + ".multigpu")
+    dev = torch.device("cuda", rank)
+    m = _mla_shards(31 + world, [5000, 1300, 64, 2049, 777], world)   # same inputs on every rank
+    t = lambda a: torch.as_tensor(np.ascontiguousarray(a), device=dev)
+    q, cache, w = t(m["q_lat"]), t(m["cache"]), t(m["w_uv"])
+    scale = 1 / np.sqrt(m["D"])
+    full = ops.latent_decode(q, cache, t(m["tables"]), t(m["lens"]),
+                             ops.plan_splits(m["lens"], m["bs"]), scale=scale, value_dim=m["Lv"],
+                             w_v=w, want_lse=True)
+    B, Hq, D = len(m["lens"]), m["Hq"], m["D"]
+    hpr = Hq // world
+    ex = mg.ShardExchange(B, Hq, m["Lv"], world, rank, dev)
+    try:
+        flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        tab, local = m["shards"][rank]
+        worst = 0.0
+        for _step in range(3):
+            plan = (ops.plan_workers(local, m["bs"], n_workers=5) if mode == "tc"
+                    else ops.plan_splits(local, m["bs"]))
+            rr = ops.latent_decode(q, cache, t(tab), t(local), plan, scale=scale,
+                                   value_dim=m["Lv"], w_v=w, mode=mode, allow_empty=True,
+                                   flags=flags, phase="partial")
+            ex.publish(rr["args"])
+            o = torch.empty((B, hpr, D), dtype=torch.float32, device=dev)
+            ls = torch.empty((B, hpr), dtype=torch.float32, device=dev)
+            ex.merge(o, w_v=w, lse_out=ls, flags=flags)
+            torch.cuda.synchronize()
+            heads = slice(rank * hpr, (rank + 1) * hpr)
+            worst = max(worst, rel_err(o.cpu(), full["ctx"][:, heads].cpu()),
+                        rel_err(ls.cpu(), full["lse"][:, heads].cpu()))
+        res = torch.tensor([worst, float(flags.item())], dtype=torch.float64, device=dev)
+        dist.all_reduce(res, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            with open(out_path, "w") as f:
+                json.dump({"err": float(res[0]), "flags": int(res[1])}, f)
+    finally:
+        ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs of one node")
+@pytest.mark.parametrize("mode", ["exact", "tc"])
+def test_shard_exchange_processes(tmp_path, mode):
+    """One process per GPU: each rank's partial pass over its block ranges,
+    the head-sharded publish into the owners' buffers over peer memory and
+    the owner's merge + W_uv equal, head for head, the unsplit decode of the
+    whole batch (exact 1e-5, tensor-core 2e-3) over three steps."""
+    world = min(torch.cuda.device_count(), 8)
+    out = tmp_path / "shard.json"
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_shard_worker, args=(r, world, port, str(out), mode))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        assert p.exitcode == 0
+    res = json.loads(out.read_text())
+    tol = 2e-3 if mode == "tc" else 1e-5
+    assert res["err"] <= tol and res["flags"] == 0
