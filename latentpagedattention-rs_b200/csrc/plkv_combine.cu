@@ -8,10 +8,6 @@
 
 namespace plkv {
 
-constexpr int kCombineRows = 8;   // (sequence, head) rows per CTA
-constexpr int kMaxWidthPerLane = 20;  // width <= 640
-constexpr int kLSlices = 8;       // latent-row slices of the projection
-constexpr int kItemBatch = 4;     // split-K items whose loads are in flight together
 
 // W is read by every step: its lines are kept in L2 (evict_last) while the
 // partial pass streams the cache through L2 with evict_first.
@@ -28,179 +24,203 @@ __device__ __forceinline__ float4 ldg_f4_keep(const float4* ptr, uint64_t pol) {
     return v;
 }
 
-// grid = (proj_heads, ceil(batch * group / kCombineRows)), block = 256.
-// Row r of the CTA is (b, h) with h = p * group + (gr % group), b = gr / group.
-// Phase 1: warp per row merges the row's items in registers (lane owns
-//   columns lane + 32k):  M = max_i m_i,  S = sum_i l_i exp(m_i - M),
-//   c[col] = sum_i ctx_i[col] exp(m_i - M) / S.
-// Phase 2: out[d] = sum_l c[l] * W[p, l, d] (lib.rs:1066-1071).  With
-//   d % 4 == 0, D <= 128 and W 16-byte aligned the 256 threads are (latent
-//   slice s) x (group of 4 columns): each thread sums its slice of l with
-//   float4 weight loads, then the slices are added in a fixed order; otherwise
-//   a column per thread.  W[p] (width x D floats) is prefetched into L2 when
-//   the CTA starts, so that its loads overlap phase 1 instead of following it.
-// Without a projection, c itself is written.
-__global__ void __launch_bounds__(256)
-combine_project_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_begin, int B,
-                       int Hq, int width, const float* __restrict__ w, int proj_heads, int D,
-                       float* __restrict__ out, float* __restrict__ lse) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    float* cs = reinterpret_cast<float*>(smem_raw);           // [kCombineRows][width]
-    float* red = cs + kCombineRows * width;                   // [kLSlices][kCombineRows][128]
-    const int group = Hq / proj_heads;
-    const int p = blockIdx.x;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rows_total = B * group;
-    const int r0 = blockIdx.y * kCombineRows;
-    const int nrows = min(kCombineRows, rows_total - r0);
-    const int ncol = (width + 31) / 32;
-    const bool vec_w = w && (D & 3) == 0 && D <= 128 &&
-                       (reinterpret_cast<uintptr_t>(w) & 15) == 0;
-    if (vec_w && tid == 0) {
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
-                     ::"l"(w + (int64_t)p * width * D), "r"((uint32_t)(width * D * 4)) : "memory");
-    }
-
-    for (int r = warp; r < kCombineRows; r += 8) {
-        float acc[kMaxWidthPerLane];
-#pragma unroll
-        for (int k = 0; k < kMaxWidthPerLane; ++k) acc[k] = 0.f;
-        float M = -INFINITY, S = 0.f;
-        int b = 0, h = 0;
-        if (r < nrows) {
-            const int gr = r0 + r;
-            b = gr / group;
-            h = p * group + gr % group;
-            const int ib = seq_item_begin[b], ie = seq_item_begin[b + 1];
-            for (int i = ib + lane; i < ie; i += 32) M = fmaxf(M, ws.part_m[(int64_t)i * Hq + h]);
-            M = warp_max(M);
-            if (M != -INFINITY) {
-                // kItemBatch items per round trip: all their loads are issued
-                // before any is used, so the row costs one memory latency per
-                // batch instead of one per item.  Items in the order i = ib..
-                for (int i0 = ib; i0 < ie; i0 += kItemBatch) {
-                    // The context loads do not wait for the item's max: an
-                    // item without tokens is skipped below, whatever its row.
-                    float wq[kItemBatch], lq[kItemBatch], v[kItemBatch][kMaxWidthPerLane];
-#pragma unroll
-                    for (int q = 0; q < kItemBatch; ++q) {
-                        const int i = i0 + q;
-                        wq[q] = i < ie ? ws.part_m[(int64_t)i * Hq + h] : -INFINITY;
-                        lq[q] = i < ie ? ws.part_l[(int64_t)i * Hq + h] : 0.f;
-                        const float* src = ws.part_ctx + ((int64_t)i * Hq + h) * width;
-#pragma unroll
-                        for (int k = 0; k < kMaxWidthPerLane; ++k) {
-                            const int col = lane + 32 * k;
-                            v[q][k] = (i < ie && k < ncol && col < width) ? src[col] : 0.f;
-                        }
-                    }
-#pragma unroll
-                    for (int q = 0; q < kItemBatch; ++q) {
-                        if (wq[q] == -INFINITY) continue;
-                        const float wi = expf(wq[q] - M);
-                        S += lq[q] * wi;
-#pragma unroll
-                        for (int k = 0; k < kMaxWidthPerLane; ++k) acc[k] = fmaf(v[q][k], wi, acc[k]);
-                    }
-                }
-            }
-        }
+// grid = ceil(B * Hq / (256 / TPR)), block = 256: the TPR / 32 warps of row
+// x * (256 / TPR) + t / TPR merge the split-K items of row (b, h)
+// (merge_row_warp), thread c = t % TPR for columns [Vc, Vc + V), [Vc + V TPR,
+// ...) ... (V = 8 with 64 threads per row when width % 8 == 0, V = 4 with
+// 128 when width % 4 == 0, else V = 1 with 128):
+//   c[col] = sum_i ctx_i[col] exp(m_i - M) / S   (lib.rs:1066-1071 input).
+// Writes dst[b, h, :] and, from thread 0 of the row, the row's M, S and lse.
+// Registers capped so that a decode batch's grid is resident at once (V = 8:
+// half the CTAs of V = 4, two per SM).
+template <int V, int TPR>
+__global__ void __launch_bounds__(256, V >= 8 ? 2 : 4)
+merge_rows_kernel(DecodeWorkspace ws, const int32_t* __restrict__ seq_item_begin, int B, int Hq,
+                  int width, float* __restrict__ dst, float* __restrict__ lse) {
+    constexpr int kRows = 256 / TPR;
+    const int64_t row = (int64_t)blockIdx.x * kRows + threadIdx.x / TPR;
+    const int c = threadIdx.x % TPR, lane = threadIdx.x & 31;
+    if (row >= (int64_t)B * Hq) return;  // whole warps: a row is TPR / 32 warps
+    const int b = (int)(row / Hq), h = (int)(row % Hq);
+    const int ib = seq_item_begin[b], ie = seq_item_begin[b + 1];
+    float M = -INFINITY, S = 0.f;
+    for (int base = 0; base < width; base += V * TPR) {   // the same passes in every lane
+        const int col = base + V * c;
+        float acc[V];
+        merge_row_warp<V>(ws, ib, ie, Hq, h, width, col, lane, acc, M, S);
         const float inv = (M != -INFINITY) ? 1.f / S : 0.f;
+        float* o = dst + row * width + col;
+        if (V % 4 == 0) {
+            if (col < width) {
 #pragma unroll
-        for (int k = 0; k < kMaxWidthPerLane; ++k) {
-            const int col = lane + 32 * k;
-            if (k < ncol && col < width) cs[r * width + col] = acc[k] * inv;
+                for (int k4 = 0; k4 < V / 4; ++k4)
+                    reinterpret_cast<float4*>(o)[k4] =
+                        make_float4(acc[4 * k4] * inv, acc[4 * k4 + 1] * inv,
+                                    acc[4 * k4 + 2] * inv, acc[4 * k4 + 3] * inv);
+            }
+        } else if (col < width) {
+            o[0] = acc[0] * inv;
         }
-        if (r < nrows && lane == 0) {
-            ws.row_m[(int64_t)b * Hq + h] = M;
-            ws.row_l[(int64_t)b * Hq + h] = S;
-            if (lse) lse[(int64_t)b * Hq + h] = (M == -INFINITY) ? -INFINITY : M + logf(S);
+    }
+    if (c == 0) {
+        ws.row_m[row] = M;
+        ws.row_l[row] = S;
+        if (lse) lse[row] = (M == -INFINITY) ? -INFINITY : M + logf(S);
+    }
+}
+
+// grid = (proj_heads, ceil(D / 32), ceil(B * group / 8)), block = 256.  The
+// CTA projects 8 rows (b, h), h = p * group + (gr % group), b = gr / group, onto
+// columns [32 y, 32 y + 32).  The rows are staged in shared memory as they
+// lie (cs[8][width], 16-byte copies).  Vector path (D % 4 == 0, W 16-byte
+// aligned): thread = (latent slice j of 32, 4 columns); slice j sums l = j,
+// j + 32, ... for all 8 rows with float4 weight loads (8 rows of weights in
+// flight per thread, each weight of the CTA loaded once), and the slices are
+// added in a fixed order: two shuffles within the warp, then the 8 warps in
+// order.  Otherwise thread (row, column) sums l in increasing order.
+__global__ void __launch_bounds__(256)
+project_rows_kernel(const float* __restrict__ rows, void* const* __restrict__ rows_table,
+                    int rows_index, size_t rows_offset, int B, int Hr, int width,
+                    const float* __restrict__ w, int proj_heads, int D, float* __restrict__ out) {
+    extern __shared__ __align__(16) float smem_f[];
+    if (rows_table)  // rows inside a buffer whose address only the device-side table holds
+        rows = reinterpret_cast<const float*>(static_cast<const char*>(rows_table[rows_index]) +
+                                              rows_offset);
+    float* cs = smem_f;                       // [8][width]
+    float* red = smem_f + (size_t)width * 8;  // [8 warps][8 rows][32]
+    const int group = Hr / proj_heads;
+    const int p = blockIdx.x, d0 = blockIdx.y * 32, r0 = blockIdx.z * 8;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nrows = min(8, B * group - r0);
+    if ((width & 3) == 0) {
+        const int w4 = width >> 2;
+        for (int r = 0; r < 8; ++r) {
+            const int gr = r0 + r;
+            const float4* src = reinterpret_cast<const float4*>(
+                rows + ((int64_t)(gr / group) * Hr + p * group + gr % group) * width);
+            for (int k = tid; k < w4; k += 256)
+                reinterpret_cast<float4*>(cs + r * width)[k] =
+                    r < nrows ? src[k] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    } else {
+        for (int idx = tid; idx < 8 * width; idx += 256) {
+            const int r = idx / width, l = idx - r * width;
+            float v = 0.f;
+            if (r < nrows) {
+                const int gr = r0 + r;
+                v = rows[((int64_t)(gr / group) * Hr + p * group + gr % group) * width + l];
+            }
+            cs[idx] = v;
         }
     }
     __syncthreads();
-
-    if (!w) {
-        for (int i = tid; i < nrows * width; i += 256) {
-            const int r = i / width, col = i - r * width;
-            const int gr = r0 + r;
-            const int b = gr / group, h = p * group + gr % group;
-            out[((int64_t)b * Hq + h) * width + col] = cs[r * width + col];
-        }
-        return;
-    }
     const float* wp = w + (int64_t)p * width * D;
-    if (vec_w) {
+    const bool vec = (D & 3) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+    if (vec) {
         const uint64_t keep = l2_evict_last_policy();
-        const int dg = tid & 31, slice = tid >> 5;
-        const int l0 = (width * slice) / kLSlices, l1 = (width * (slice + 1)) / kLSlices;
-        float acc[kCombineRows][4];
+        const int lsub = lane >> 3, dq = lane & 7;
+        const int slice = warp * 4 + lsub;
+        const int dcol = d0 + 4 * dq;
+        float acc[8][4];
 #pragma unroll
-        for (int r = 0; r < kCombineRows; ++r)
+        for (int r = 0; r < 8; ++r)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
-        if (4 * dg < D) {
-#pragma unroll 16
-            for (int l = l0; l < l1; ++l) {
-                const float4 wv = ldg_f4_keep(reinterpret_cast<const float4*>(wp + (int64_t)l * D) + dg, keep);
+        if (dcol < D) {
+            for (int l0 = slice; l0 < width; l0 += 32 * 8) {
+                float4 wv[8];
 #pragma unroll
-                for (int r = 0; r < kCombineRows; ++r) {
-                    const float c = cs[r * width + l];
-                    acc[r][0] = fmaf(c, wv.x, acc[r][0]);
-                    acc[r][1] = fmaf(c, wv.y, acc[r][1]);
-                    acc[r][2] = fmaf(c, wv.z, acc[r][2]);
-                    acc[r][3] = fmaf(c, wv.w, acc[r][3]);
+                for (int u = 0; u < 8; ++u) {
+                    const int l = l0 + 32 * u;
+                    wv[u] = l < width ? ldg_f4_keep(reinterpret_cast<const float4*>(
+                                                        wp + (int64_t)l * D + dcol), keep)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int l = l0 + 32 * u;
+                    if (l >= width) break;
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) {
+                        const float c = cs[r * width + l];
+                        acc[r][0] = fmaf(c, wv[u].x, acc[r][0]);
+                        acc[r][1] = fmaf(c, wv[u].y, acc[r][1]);
+                        acc[r][2] = fmaf(c, wv[u].z, acc[r][2]);
+                        acc[r][3] = fmaf(c, wv[u].w, acc[r][3]);
+                    }
                 }
             }
+        }
 #pragma unroll
-            for (int r = 0; r < kCombineRows; ++r)
-                *reinterpret_cast<float4*>(red + (slice * kCombineRows + r) * 128 + 4 * dg) =
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                acc[r][e] += __shfl_xor_sync(0xffffffffu, acc[r][e], 8);
+                acc[r][e] += __shfl_xor_sync(0xffffffffu, acc[r][e], 16);
+            }
+        if (lsub == 0) {
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                *reinterpret_cast<float4*>(red + (warp * 8 + r) * 32 + 4 * dq) =
                     make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
         }
         __syncthreads();
-        for (int i = tid; i < nrows * D; i += 256) {
-            const int r = i / D, d = i - r * D;
+        const int r = warp, d = d0 + lane;
+        if (r < nrows && d < D) {
             float v = 0.f;
 #pragma unroll
-            for (int sl = 0; sl < kLSlices; ++sl) v += red[(sl * kCombineRows + r) * 128 + d];
+            for (int k = 0; k < 8; ++k) v += red[(k * 8 + r) * 32 + lane];
             const int gr = r0 + r;
-            const int b = gr / group, h = p * group + gr % group;
-            out[((int64_t)b * Hq + h) * D + d] = v;
+            out[((int64_t)(gr / group) * Hr + p * group + gr % group) * D + d] = v;
         }
         return;
     }
-    for (int d0 = 0; d0 < D; d0 += 256) {
-        const int d = d0 + tid;
-        if (d >= D) continue;
-        float acc[kCombineRows];
-#pragma unroll
-        for (int r = 0; r < kCombineRows; ++r) acc[r] = 0.f;
-        for (int l = 0; l < width; ++l) {
-            const float wv = wp[(int64_t)l * D + d];
-#pragma unroll
-            for (int r = 0; r < kCombineRows; ++r) acc[r] = fmaf(cs[r * width + l], wv, acc[r]);
-        }
-        for (int r = 0; r < nrows; ++r) {
+    const int d = d0 + lane;
+    if (d < D) {
+        for (int r = warp; r < nrows; r += 8) {
+            float v = 0.f;
+            for (int l = 0; l < width; ++l) v = fmaf(cs[r * width + l], wp[(int64_t)l * D + d], v);
             const int gr = r0 + r;
-            const int b = gr / group, h = p * group + gr % group;
-            out[((int64_t)b * Hq + h) * D + d] = acc[r];
+            out[((int64_t)(gr / group) * Hr + p * group + gr % group) * D + d] = v;
         }
     }
 }
 
+cudaError_t launch_project_rows(const float* rows, void* const* rows_table, int rows_index,
+                                size_t rows_offset, int B, int Hr, int width, const float* w,
+                                int proj_heads, int D, float* out, cudaStream_t st) {
+    const int group = Hr / proj_heads;
+    const size_t smem = (size_t)width * 8 * 4 + 8 * 8 * 32 * 4;
+    cudaError_t e = cudaFuncSetAttribute(project_rows_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(proj_heads, (D + 31) / 32, (B * group + 7) / 8);
+    project_rows_kernel<<<grid, 256, smem, st>>>(rows, rows_table, rows_index, rows_offset, B, Hr,
+                                                 width, w, proj_heads, D, out);
+    return cudaGetLastError();
+}
+
+// Split-K combine: merge_rows (items -> normalised rows), then, with a
+// projection, project_rows (rows -> out).
 cudaError_t launch_combine(DecodeWorkspace ws, const int32_t* seq_item_begin, int B, int Hq,
                            int width, const float* w, int proj_heads, int D, float* out,
                            float* lse, cudaStream_t st) {
     if (!w) proj_heads = Hq;
-    if (width > 32 * kMaxWidthPerLane) return cudaErrorInvalidValue;
-    const int group = Hq / proj_heads;
-    const size_t smem = size_t(kCombineRows) * width * 4 + size_t(kLSlices) * kCombineRows * 128 * 4;
-    cudaError_t e = cudaFuncSetAttribute(combine_project_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid(proj_heads, (B * group + kCombineRows - 1) / kCombineRows);
-    combine_project_kernel<<<grid, 256, smem, st>>>(ws, seq_item_begin, B, Hq, width, w,
-                                                     proj_heads, D, out, lse);
-    return cudaGetLastError();
+    float* dst = w ? ws.row_ctx : out;
+    const int64_t rows = (int64_t)B * Hq;
+    if ((width & 7) == 0)
+        merge_rows_kernel<8, 64><<<(unsigned)((rows + 3) / 4), 256, 0, st>>>(
+            ws, seq_item_begin, B, Hq, width, dst, lse);
+    else if ((width & 3) == 0)
+        merge_rows_kernel<4, 128><<<(unsigned)((rows + 1) / 2), 256, 0, st>>>(
+            ws, seq_item_begin, B, Hq, width, dst, lse);
+    else
+        merge_rows_kernel<1, 128><<<(unsigned)((rows + 1) / 2), 256, 0, st>>>(
+            ws, seq_item_begin, B, Hq, width, dst, lse);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || !w) return e;
+    return launch_project_rows(ws.row_ctx, nullptr, 0, 0, B, Hq, width, w, proj_heads, D, out,
+                               st);
 }
 
 // grid = batch * q_heads rows, block = 256: probabilities from the stored

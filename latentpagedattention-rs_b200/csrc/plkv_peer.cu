@@ -50,11 +50,6 @@ constexpr int kMaxPeers = 32;    // one lane per rank in the merge
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
-    uint64_t v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
 
 // Bytes of one slot, padded to 256 so that both slots start 16-byte aligned
 // (the publish copy stores float4).
@@ -126,26 +121,17 @@ merge_kernel(int64_t rows, int width, void* const* __restrict__ bufs, int world,
     const uint64_t e = ctrl[0] + 1;
     const int parity = (int)(e & 1);
     __shared__ int ok_s;
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        for (int s = 0; s < world && ok; ++s) {
-            if (!fits(bufs[s], rows, width)) {
-                if (blockIdx.x == 0) set_flag(flags, PLKV_FLAG_BAD_POSITION);
-                ok = 0;
-            }
+    if (threadIdx.x < 32) {
+        const bool fit = threadIdx.x >= world || fits(bufs[threadIdx.x], rows, width);
+        const bool all_fit = __all_sync(0xffffffffu, fit);
+        if (!all_fit && blockIdx.x == 0 && threadIdx.x == 0) set_flag(flags, PLKV_FLAG_BAD_POSITION);
+        // every rank's flag polled at once (bounded)
+        const bool arrived = sm100::wait_flags_warp(static_cast<const uint64_t*>(bufs[rank]),
+                                                    all_fit ? world : 0, e);
+        if (threadIdx.x == 0) {
+            if (!arrived) set_flag(flags, PLKV_FLAG_TIMEOUT);
+            ok_s = all_fit && arrived;
         }
-        const uint64_t* f = static_cast<const uint64_t*>(bufs[rank]);
-        const uint64_t t0 = sm100::globaltimer();
-        for (int s = 0; s < world && ok; ++s) {
-            while (ld_acquire_sys(f + s) < e) {
-                if (sm100::globaltimer() - t0 > sm100::kWaitLimitNs) {
-                    set_flag(flags, PLKV_FLAG_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        ok_s = ok;
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

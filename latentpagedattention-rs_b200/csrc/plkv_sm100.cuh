@@ -200,6 +200,26 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Called by a whole warp: lane s < n waits until flags[s] >= e (system-scope
+// acquire loads, so the writes released before each flag are visible to the
+// warp and, after a CTA barrier, to the CTA).  All flags are polled together;
+// the wait gives up after kWaitLimitNs.  Returns (warp-uniformly) whether
+// every flag arrived.
+__device__ __forceinline__ bool wait_flags_warp(const uint64_t* flags, int n, uint64_t e) {
+    const int lane = threadIdx.x & 31;
+    bool done = lane >= n, gave_up = false;
+    const uint64_t t0 = globaltimer();
+    while (!__all_sync(0xffffffffu, done || gave_up)) {
+        if (!done && !gave_up) {
+            uint64_t v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + lane) : "memory");
+            done = v >= e;
+            if (!done && globaltimer() - t0 > kWaitLimitNs) gave_up = true;
+        }
+    }
+    return !__any_sync(0xffffffffu, gave_up);
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
