@@ -445,7 +445,7 @@ def run_ours(args, s, rank: int, world: int):
 
         flags = loop.flags
 
-        def run_step(ev=None):
+        def run_step(ev=None, marks=None):
             if ev is not None:
                 loop.partial_events = [ev]
             r = loop.step()[0]
@@ -517,7 +517,7 @@ def run_ours(args, s, rank: int, world: int):
 
         q_buf, rows_buf = q_in, new_rows
 
-        def run_step(ev=None):
+        def run_step(ev=None, marks=None):
             return step(q_buf, rows_buf, ev)
 
         # append, (reconstruction), full-KV partial + combine, W_o GEMM + reduction
@@ -584,12 +584,23 @@ def run_ours(args, s, rank: int, world: int):
                                        flags=flags)
             return ops.out_proj(a, w, out=out, k_splits=wo_splits, workspace=wo_ws)
 
-        def step(q_src, rows_src, ev=None):
+        def step(q_src, rows_src, ev=None, marks=None):
+            def mark(name):
+                # phase boundaries of the eager steps (CUDA events on the stream)
+                if marks is not None:
+                    e = torch.cuda.Event(enable_timing=True)
+                    e.record()
+                    marks.append((name, e))
+
+            mark("start")
             if split_k:
                 ops.latent_append_slots(rows_src, x["cache"], slots_d, flags=flags)
             else:
                 ops.latent_append(rows_src, x["cache"], tables, positions=positions, flags=flags)
+            mark("append")
             q_lat = q_src if s.absorbed else ops.project_query(q_src, x["w_k"], out=q_lat_buf)
+            if not s.absorbed:
+                mark("project_query")
             if ev is not None:
                 ev[0].record()
             r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
@@ -598,41 +609,51 @@ def run_ours(args, s, rank: int, world: int):
                                   flags=flags, phase="partial")
             if ev is not None:
                 ev[1].record()
+            mark("partial (q staging + decode)")
             if shard_x is not None:
                 # head-sharded merge: this rank's heads only, W_uv of those heads
                 shard_x.publish(r["args"])
+                mark("shard publish")
                 res = shard_x.merge(res_shard, w_v=x["w_v"], flags=flags)
+                mark("shard merge + W_uv")
                 last["ctx"] = res
                 if w_o is not None:
                     res = project(res.reshape(nb_local, -1), w_o)
+                    mark("W_o (row shard)")
                     dist.all_reduce(res)
+                    mark("W_o all-reduce")
                 return res
             r = ops.latent_decode(q_lat, x["cache"], tables, lens, plan, scale=s.scale,
                                   value_dim=s.value_dim, w_v=x["w_v"], mode=mode, out=ctx,
                                   want_lse=want_lse, workspace=ws, allow_empty=split_k,
                                   flags=flags, phase="combine")
+            mark("combine + W_uv")
             res = ctx
             if split_k and peer_x is not None:
                 peer_x.publish(ctx, r["lse"], flags=flags)
                 res = peer_x.merge(merged, flags=flags)
+                mark("peer exchange")
             elif split_k:
                 res = mg.gather_and_merge(ctx, r["lse"], world,
                                           lambda c, l: ops.lse_merge(c, l, out=merged_nccl)[0],
                                           gathered_ctx, gathered_lse)
+                mark("NCCL exchange")
             last["ctx"] = res
             if w_o is not None and wo_sharded:
                 rows = (res.reshape(B, -1) if split_k else
                         mg.gather_rows(res.reshape(nb_local, -1), world, max_rows,
                                        gathered=g_rows).reshape(-1, K_o))
                 res = mg.sharded_out_proj(rows, w_o, world, project, gathered=g_out)
+                mark("W_o (sharded)")
             elif w_o is not None:
                 res = project(res.reshape(nb_local, -1), w_o)
+                mark("W_o")
             return res
 
         q_buf, rows_buf = q_in, new_rows
 
-        def run_step(ev=None):
-            return step(q_buf, rows_buf, ev)
+        def run_step(ev=None, marks=None):
+            return step(q_buf, rows_buf, ev, marks)
 
         # append, partial pass (+ FP16 query staging in tensor-core mode),
         # combine, query projection, shard merge (peer exchange: publish +
@@ -669,14 +690,20 @@ def run_ours(args, s, rank: int, world: int):
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     timed_from = steps_done
+    step_marks = [[] for _ in range(args.steps)]
     start.record()
     for i in range(args.steps):
-        run_step(kev[i])
+        run_step(kev[i], step_marks[i])
     end.record()
     barrier()
     steps_done += args.steps
     eager_ms = start.elapsed_time(end)
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    # Mean device time of each phase of the eager steps (between consecutive
+    # marks); the max over ranks is taken below.
+    phase_names = [n for n, _ in step_marks[0][1:]] if step_marks[0] else []
+    phase_us = [statistics.mean(m[k][1].elapsed_time(m[k + 1][1]) * 1e3 for m in step_marks)
+                for k in range(len(phase_names))]
     elapsed_ms = eager_ms
     stepper = run_step
     graph = None
@@ -719,10 +746,11 @@ def run_ours(args, s, rank: int, world: int):
         steps_done += args.steps
         elapsed_ms = g0.elapsed_time(g1)
     clock_info = clocks.stop() if clocks else None
-    t = torch.tensor([elapsed_ms, kern_ms, eager_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([elapsed_ms, kern_ms, eager_ms] + phase_us, dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms, kern_ms, eager_ms = float(t[0]), float(t[1]), float(t[2])
+    phases = {n: round(float(v), 1) for n, v in zip(phase_names, t[3:].tolist())}
     ms_per_step = elapsed_ms / args.steps
     # Lengths attended in the middle of the timed steps (they grow by one a
     # step with --grow).
@@ -827,7 +855,9 @@ def run_ours(args, s, rank: int, world: int):
                     "exchange": (args.exchange if split_k else None),
                     "parallelism": (f"split-k{world}" if split_k else
                                     (f"dp{world}" if world > 1 else "single")),
-                    "work_items": plan.n_items},
+                    "work_items": plan.n_items,
+                    # device time of each phase of an eager step, max over ranks
+                    "phases_us_eager": phases},
             "roofline": roofline, "gpu_launches": launches_per_step * args.steps,
             "clocks": clock_info, "parity": parity, "err_flags": err_flags,
             # persistent cache of the attended tokens: the latent pool against the

@@ -307,11 +307,13 @@ int plkv_latent_decode_noalloc(const plkv_latent_decode_args* args, plkv_stream_
  * split-K each rank decodes its range of every sequence's blocks with
  * plkv_latent_decode_partial; instead of the combine, plkv_shard_publish
  * merges the rank's work items per (sequence, head) into a normalised latent
- * context and log-sum-exp and stores them into the buffer of the rank that
- * owns the head (rank r owns heads [r H/W, (r+1) H/W)).  plkv_shard_merge
- * then waits (bounded, 1 s: PLKV_FLAG_TIMEOUT, rows 0 and lse -inf) for every
- * rank's publish of the step, merges the W sources with the LSE rule and
- * applies W_v / W_uv of the owned heads: out[batch, H/W, head_dim] and
+ * context and log-sum-exp, stores them into this rank's own buffer and
+ * releases this rank's flag in every rank's buffer.  Rank r owns heads
+ * [r H/W, (r+1) H/W).  plkv_shard_merge then waits (bounded, 1 s:
+ * PLKV_FLAG_TIMEOUT, rows 0 and lse -inf) for every rank's publish of the
+ * step, reads the owned heads' rows from every rank's buffer (peer loads),
+ * merges the W sources with the LSE rule and applies W_v / W_uv of the owned
+ * heads: out[batch, H/W, head_dim] and
  * lse_out[batch, H/W] (may be NULL) hold the merged result of this rank's
  * heads; w_v NULL writes the latent context (width value_dim).  Buffers of
  * plkv_shard_buffer_bytes(batch, q_heads, value_dim) bytes come from
@@ -319,7 +321,7 @@ int plkv_latent_decode_noalloc(const plkv_latent_decode_args* args, plkv_stream_
  * described for the peer exchange above: bufs a DEVICE array of the W base
  * pointers, ctrl a zeroed DEVICE array of 4 uint64 of this rank, every rank
  * issuing the same steps with the same shapes; q_heads % world == 0; world
- * <= 32; value_dim <= 640.  publish reads args->workspace (the partial pass's
+ * <= 32.  publish reads args->workspace (the partial pass's
  * results), seq_item_begin, batch, q_heads, latent_dim, value_dim, n_items
  * and err_flags. */
 size_t plkv_shard_buffer_bytes(int32_t batch, int32_t q_heads, int32_t value_dim);
