@@ -28,6 +28,9 @@ bool tc_supported(const plkv_latent_decode_args&);
 cudaError_t launch_latent_partial_tc2(const plkv_latent_decode_args&, DecodeWorkspace,
                                       cudaStream_t);
 bool tc2_supported(const plkv_latent_decode_args&);
+bool fullkv_tc_supported(const plkv_fullkv_decode_args&);
+cudaError_t launch_fullkv_partial_tc(const plkv_fullkv_decode_args&, DecodeWorkspace,
+                                     cudaStream_t);
 cudaError_t launch_fullkv_partial_exact(const plkv_fullkv_decode_args&, DecodeWorkspace,
                                         cudaStream_t);
 cudaError_t launch_project_query(const float*, const float*, float*, int, int, int, int, int,
@@ -432,7 +435,12 @@ int plkv_fullkv_decode(const plkv_fullkv_decode_args* a, plkv_stream_t stream) {
     DecodeWorkspace ws = carve_workspace(a->workspace, a->n_items, a->batch, a->q_heads, 0,
                                          a->head_dim);
     cudaStream_t s = (cudaStream_t)stream;
-    PLKV_CUDA_CHECK(launch_fullkv_partial_exact(*a, ws, s));
+    // head_dim 128 and <= 16 query heads per KV head without intermediates run
+    // on the tensor cores (FP32-accurate: Q and P split into FP16 hi + lo)
+    if (fullkv_tc_supported(*a))
+        PLKV_CUDA_CHECK(launch_fullkv_partial_tc(*a, ws, s));
+    else
+        PLKV_CUDA_CHECK(launch_fullkv_partial_exact(*a, ws, s));
     PLKV_CUDA_CHECK(launch_combine(ws, a->seq_item_begin, a->batch, a->q_heads, a->head_dim,
                                    nullptr, a->q_heads, a->head_dim, a->ctx, a->lse, s));
     if (a->scores)

@@ -1,0 +1,514 @@
+// plkv_fullkv_tc.cu -- tensor-core (tcgen05) split-K partial pass of the FP16
+// full-KV paged GQA decode (the baseline of lib.rs:1147-1269,
+// attention_ref.py:172-224) for head_dim 128 and up to 16 query heads per KV
+// head.
+//
+// Same contract as fullkv_partial_exact_kernel (plkv_decode_exact.cu): every
+// (work item, KV head g) emits per query head h = g G + i the running max m
+// (natural-log units), the sum l of exp(score - m) and the unnormalised
+// context sum_t exp(score_t - m) V_t; the shared combine merges the items.
+//
+// The G query heads of one KV head are too few rows for a tcgen05 tile, so the
+// tokens are the rows:
+//   S^T = K . Q^T   M = 128 tokens, N = 16 (the G heads, padded), K = 128 dims
+//   O^T = V^T . P^T M = 128 dims,   N = 16,                        K = 128 tokens
+// both cta_group::1 kind::f16 with FP32 accumulators in tensor memory (S^T
+// double-buffered, O^T resident for the item).  K and V are FP16 as stored,
+// so only Q and P need care to keep FP32 accuracy: each is split into an FP16
+// high part and an FP16 low part (x = hi + lo + O(2^-22 x)) and multiplied
+// twice; FP16 x FP16 products are exact in FP32, so scores and context carry
+// FP32 accumulation error only (~1e-7 relative; the exact-mode bar is 1e-5).
+//
+// Data movement: the K and V rows of a tile are gathered by two loader warps
+// with 16-byte cp.async copies straight into the 128-byte-swizzled operand
+// layouts (K: K-major [2 column blocks][128 rows][128 B]; V is the same bytes
+// read as the MN-major A operand V^T), three 64 KiB stages in flight.  Rows
+// of a block are 256 contiguous bytes of the head-major pool, so a warp copies
+// two rows = 512 contiguous bytes per instruction; blocks of 16 rows would
+// need 16 TMA boxes per tile and operand.  Rows past the item's end, or of a
+// table entry outside the pool, are zeroed instead (0 x garbage must stay 0 in
+// the context MMA).
+//
+// Softmax: TMEM lane = token; per head a warp-shuffle max over the lanes and
+// the four warps through shared memory; log2 domain with a lazily updated
+// running max (threshold 8: probabilities stay <= 2^8), O^T rescaled in TMEM
+// only when a head's max moved by more than that.
+//
+// Warps: 0-3 softmax and epilogue, 4 tensor-memory allocation and (lane 0)
+// MMA issue, 5-6 loaders.  Every wait is bounded (1 s): on expiry the kernel
+// records PLKV_FLAG_TIMEOUT, abandons its work and frees tensor memory.
+#include <cuda_fp16.h>
+
+#include "plkv_sm100.cuh"
+
+namespace plkv {
+namespace fkv {
+
+constexpr int kTok = 128;        // tokens per tile
+constexpr int kD = 128;          // head_dim
+constexpr int kN = 16;           // query heads of a KV head, padded
+constexpr int kStages = 3;
+constexpr uint32_t kHalf = kTok * 128;             // 64 columns x 128 rows: 16 KiB
+constexpr uint32_t kTileBytes = 2 * kHalf;          // K or V tile: 32 KiB
+constexpr uint32_t kStageBytes = 2 * kTileBytes;    // K + V: 64 KiB
+constexpr uint32_t kOpBlock = kN * 128;             // 64 columns x 16 rows: 2 KiB
+constexpr uint32_t kOpBytes = 2 * kOpBlock;         // a 16 x 128 FP16 operand: 4 KiB
+constexpr uint32_t kKVOff = 0;
+constexpr uint32_t kQOff = kKVOff + kStages * kStageBytes;  // Q hi, Q lo
+constexpr uint32_t kPOff = kQOff + 2 * kOpBytes;            // [2 buffers][hi, lo]
+constexpr uint32_t kMiscOff = kPOff + 4 * kOpBytes;
+constexpr uint32_t kMiscBytes = 1024;
+constexpr uint32_t kSmemBytes = kMiscOff + kMiscBytes;      // 222208
+constexpr uint32_t kTmemCols = 64;
+constexpr uint32_t kColS = 0;    // S^T buffers at columns 0 and 16
+constexpr uint32_t kColO = 32;   // O^T
+constexpr int kLoaders = 64;
+constexpr int kThreads = 224;
+constexpr float kTau = 8.f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+enum : uint32_t {
+    kBarKVFull = 0,                          // [kStages] loaders: the tile's K and V landed
+    kBarKVEmpty = kBarKVFull + 8 * kStages,  // [kStages] MMA commit: S and O of the tile done
+    kBarSFull = kBarKVEmpty + 8 * kStages,   // [2] MMA commit: S^T of the tile in TMEM
+    kBarPFull = kBarSFull + 16,              // [2] softmax: P of the tile written
+    kBarODone = kBarPFull + 16,              // [2] MMA commit: O^T through the tile done
+    kTmemSlot = kBarODone + 16,
+    kAbort = kTmemSlot + 4,
+    kRedMax = 256,                           // [4 warps][16] float
+    kRedSum = kRedMax + 256,                 // [4 warps][16] float
+};
+static_assert(kAbort + 4 <= kRedMax, "barriers");
+static_assert(kRedSum + 256 <= kMiscBytes, "misc region");
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(dst_smem), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                 ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns: thread i of the warp gets lane
+// (warp's quarter * 32 + i), columns [col, col + 16).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
+    uint32_t r[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(v[i]);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+          "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),
+          "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void st_shared_zero16(uint32_t dst) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+}
+
+__device__ __forceinline__ void named_sync_softmax() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Byte offset of element (row, k) of a 16-row FP16 operand stored K-major in
+// 128-byte-swizzled 64-column blocks (Q^T's and P^T's rows are the heads).
+__device__ __forceinline__ uint32_t op_offset(int row, int k) {
+    return (uint32_t)(k >> 6) * kOpBlock + (uint32_t)(row >> 3) * 1024u +
+           (uint32_t)(row & 7) * 128u + ((((uint32_t)(k & 63) >> 3) ^ (uint32_t)(row & 7)) << 4) +
+           (uint32_t)(k & 7) * 2u;
+}
+
+// grid = (n_items, KV heads), block = 224, one CTA per SM (222 KiB).
+__global__ void __launch_bounds__(kThreads, 1)
+fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict__ k_cache,
+                         const uint16_t* __restrict__ v_cache, int64_t num_physical, int KV,
+                         int bs, int Hq, float scale_log2, const int32_t* __restrict__ tables,
+                         int64_t max_blocks, const int32_t* __restrict__ seq_lens,
+                         const plkv_work_item* __restrict__ items, DecodeWorkspace ws,
+                         int32_t* flags) {
+    using namespace sm100;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t sbase = smem_u32(smem);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (sbase & 1023u) {  // the swizzled operands need 1 KiB alignment
+        if (tid == 0) set_flag(flags, PLKV_FLAG_TIMEOUT);
+        return;
+    }
+    const plkv_work_item it = items[blockIdx.x];
+    const int b = it.seq, g = blockIdx.y;
+    const int G = Hq / KV;
+    int len = seq_lens[b];
+    const int64_t cap = max_blocks * (int64_t)bs;
+    if (len < 0 || len > cap) {
+        if (tid == 0 && g == 0) set_flag(flags, PLKV_FLAG_BAD_LENGTH);
+        len = len < 0 ? 0 : (int)cap;
+    }
+    const int t_begin = it.block_begin * bs;
+    const int t_end = max(t_begin, min(it.block_end * bs, len));
+    const int n_tiles = (t_end - t_begin + kTok - 1) / kTok;
+
+    uint8_t* misc = smem + kMiscOff;
+    const uint32_t mb = sbase + kMiscOff;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + kAbort);
+    const WaitCtx wc{flags, ws.ctl, abort_flag};
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(mb + kBarKVFull + 8 * s, kLoaders);
+            mbar_init(mb + kBarKVEmpty + 8 * s, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(mb + kBarSFull + 8 * i, 1);
+            mbar_init(mb + kBarPFull + 8 * i, 1);
+            mbar_init(mb + kBarODone + 8 * i, 1);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    // Q^T as high and low FP16 parts (rows >= G zero), both P buffers zero.
+    for (int i = tid; i < kN * kD; i += kThreads) {
+        const int h = i / kD, d = i - h * kD;
+        const float x = h < G ? q[((int64_t)b * Hq + g * G + h) * kD + d] : 0.f;
+        const __half hi = __float2half_rn(x);
+        const __half lo = __float2half_rn(x - __half2float(hi));
+        const uint32_t off = op_offset(h, d);
+        *reinterpret_cast<__half*>(smem + kQOff + off) = hi;
+        *reinterpret_cast<__half*>(smem + kQOff + kOpBytes + off) = lo;
+    }
+    for (int i = tid; i < (int)(4 * kOpBytes / 16); i += kThreads)
+        reinterpret_cast<uint4*>(smem + kPOff)[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+    if (warp == 4) {
+        tmem_alloc(mb + kTmemSlot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(misc + kTmemSlot);
+
+    if (warp >= 5) {
+        // ------------------------------------------------------------ loaders
+        const int li = tid - 160;
+        const int chunk = li & 15, rsub = li >> 4;   // 16-byte chunk of a row; row phase
+        const int cb = chunk >> 3, cc = chunk & 7;
+        auto issue = [&](int j) {
+            const uint32_t kdst = sbase + kKVOff + (uint32_t)(j % kStages) * kStageBytes;
+            const uint32_t vdst = kdst + kTileBytes;
+            const int t0 = t_begin + j * kTok;
+#pragma unroll 4
+            for (int k = 0; k < kTok / 4; ++k) {
+                const int r = rsub + 4 * k;
+                const int t = t0 + r;
+                const uint32_t off = (uint32_t)cb * kHalf + (uint32_t)(r >> 3) * 1024u +
+                                     (uint32_t)(r & 7) * 128u +
+                                     (((uint32_t)cc ^ (uint32_t)(r & 7)) << 4);
+                int64_t src = -1;
+                if (t < t_end) {
+                    const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
+                    if (phys >= 0 && phys < num_physical)
+                        src = (((int64_t)phys * KV + g) * bs + (t % bs)) * kD + chunk * 8;
+                    else if (g == 0 && chunk == 0)
+                        set_flag(flags, PLKV_FLAG_BAD_BLOCK);
+                }
+                if (src >= 0) {
+                    cp_async16(kdst + off, k_cache + src);
+                    cp_async16(vdst + off, v_cache + src);
+                } else {
+                    st_shared_zero16(kdst + off);
+                    st_shared_zero16(vdst + off);
+                }
+            }
+            cp_async_commit();
+        };
+        bool ok = true;
+        for (int j = 0; j < kStages - 1; ++j) {
+            if (j < n_tiles) issue(j);
+            else cp_async_commit();
+        }
+        for (int j = 0; ok && j < n_tiles; ++j) {
+            cp_async_wait<kStages - 2>();   // this thread's copies of tile j landed
+            fence_proxy_async_smem();       // ... and are visible to the tensor core
+            mbar_arrive_local(mb + kBarKVFull + 8 * (j % kStages));
+            const int jn = j + kStages - 1;
+            if (jn < n_tiles) {
+                // the stage held tile jn - kStages, read by its S and O
+                if (jn >= kStages &&
+                    !(ok = mbar_wait(mb + kBarKVEmpty + 8 * (jn % kStages),
+                                     ((jn / kStages) - 1) & 1, wc)))
+                    break;
+                issue(jn);
+            } else {
+                cp_async_commit();
+            }
+        }
+        cp_async_wait<0>();
+    } else if (warp == 4) {
+        // --------------------------------------------------------- MMA issue
+        if (lane == 0 && n_tiles > 0) {
+            const uint32_t id_s = idesc_f16(128, kN, false, false);
+            const uint32_t id_o = idesc_f16(128, kN, true, false);
+            auto issue_s = [&](int j) -> bool {
+                const int st = j % kStages, sb = j & 1;
+                if (!mbar_wait(mb + kBarKVFull + 8 * st, (j / kStages) & 1, wc)) return false;
+                // S buffer sb was last read by the softmax of tile j - 2
+                if (j >= 2 && !mbar_wait(mb + kBarPFull + 8 * sb, ((j - 2) >> 1) & 1, wc))
+                    return false;
+                tc_fence_after();
+                const uint32_t kt = sbase + kKVOff + (uint32_t)st * kStageBytes;
+#pragma unroll
+                for (int kk = 0; kk < kD / 16; ++kk) {
+                    const uint32_t koff = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
+                    const uint32_t qoff = (uint32_t)(kk >> 2) * kOpBlock + (uint32_t)(kk & 3) * 32u;
+                    const uint64_t a = sdesc_sw128(kt + koff, 16, 1024);
+                    mma_f16(tmem + kColS + 16 * sb, a, sdesc_sw128(sbase + kQOff + qoff, 16, 1024),
+                            id_s, kk > 0 ? 1u : 0u);
+                    mma_f16(tmem + kColS + 16 * sb, a,
+                            sdesc_sw128(sbase + kQOff + kOpBytes + qoff, 16, 1024), id_s, 1u);
+                }
+                mma_commit(mb + kBarSFull + 8 * sb);
+                return true;
+            };
+            auto issue_o = [&](int j) -> bool {
+                const int st = j % kStages, pb = j & 1;
+                if (!mbar_wait(mb + kBarPFull + 8 * pb, (j >> 1) & 1, wc)) return false;
+                tc_fence_after();
+                const uint32_t vt = sbase + kKVOff + (uint32_t)st * kStageBytes + kTileBytes;
+                const uint32_t pbase = sbase + kPOff + (uint32_t)pb * 2u * kOpBytes;
+#pragma unroll
+                for (int kt = 0; kt < kTok / 16; ++kt) {
+                    // V^T: MN-major, 64-dim blocks kHalf apart, 8-token groups 1 KiB apart
+                    const uint64_t a = sdesc_sw128(vt + (uint32_t)kt * 2048u, kHalf, 1024);
+                    const uint32_t poff = (uint32_t)(kt >> 2) * kOpBlock + (uint32_t)(kt & 3) * 32u;
+                    mma_f16(tmem + kColO, a, sdesc_sw128(pbase + poff, 16, 1024), id_o,
+                            (j > 0 || kt > 0) ? 1u : 0u);
+                    mma_f16(tmem + kColO, a, sdesc_sw128(pbase + kOpBytes + poff, 16, 1024), id_o,
+                            1u);
+                }
+                mma_commit(mb + kBarODone + 8 * pb);
+                mma_commit(mb + kBarKVEmpty + 8 * st);
+                return true;
+            };
+            bool ok = issue_s(0);
+            for (int j = 0; ok && j < n_tiles; ++j) {
+                if (j + 1 < n_tiles) ok = issue_s(j + 1);
+                if (ok) ok = issue_o(j);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ softmax and epilogue
+        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        float* red_max = reinterpret_cast<float*>(misc + kRedMax);
+        float* red_sum = reinterpret_cast<float*>(misc + kRedSum);
+        float m_use[kN], l_w[kN];
+#pragma unroll
+        for (int h = 0; h < kN; ++h) {
+            m_use[h] = -INFINITY;
+            l_w[h] = 0.f;
+        }
+        bool ok = true;
+        // Every softmax thread runs every iteration and reaches every named
+        // barrier; after a failed wait it only skips the work.
+        for (int j = 0; j < n_tiles; ++j) {
+            const int sb = j & 1;
+            // This thread's token: inside the item and of a block inside the
+            // pool (the loaders zeroed the rows of any other), looked up
+            // before the wait so that the load overlaps it.
+            const int t = t_begin + j * kTok + tid;
+            bool tok_ok = t < t_end;
+            if (tok_ok) {
+                const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
+                tok_ok = phys >= 0 && phys < num_physical;
+            }
+            if (ok)
+                ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarSFull + 8 * sb, (j >> 1) & 1, wc));
+            float s[kN];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld16(tmem + lane_base + kColS + 16 * sb, s);
+                tmem_wait_ld();
+            }
+            const bool valid = ok && tok_ok;
+#pragma unroll
+            for (int h = 0; h < kN; ++h) {
+                s[h] = (valid && h < G) ? s[h] * scale_log2 : -INFINITY;
+                if (h < G) {
+                    const float mx = warp_max(s[h]);
+                    if (lane == 0) red_max[warp * kN + h] = mx;
+                }
+            }
+            named_sync_softmax();
+            float alpha[kN];
+            bool resc = false;
+#pragma unroll
+            for (int h = 0; h < kN; ++h) {
+                alpha[h] = 1.f;
+                if (h < G) {
+                    const float mt = fmaxf(fmaxf(red_max[h], red_max[kN + h]),
+                                           fmaxf(red_max[2 * kN + h], red_max[3 * kN + h]));
+                    const float m_new = fmaxf(m_use[h], mt);
+                    if (m_new > m_use[h] + kTau) {
+                        alpha[h] = (m_use[h] == -INFINITY) ? 0.f : fast_exp2(m_use[h] - m_new);
+                        m_use[h] = m_new;
+                        l_w[h] *= alpha[h];
+                        resc = true;
+                    }
+                }
+            }
+            float p[kN];
+#pragma unroll
+            for (int h = 0; h < kN; ++h) {
+                p[h] = (h < G && s[h] != -INFINITY) ? fast_exp2(s[h] - m_use[h]) : 0.f;
+                if (h < G) l_w[h] += warp_sum(p[h]);
+            }
+            if (ok && resc && j > 0) {
+                // O^T through tile j - 1 must be complete before it is rescaled
+                ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * ((j - 1) & 1),
+                                                       ((j - 1) >> 1) & 1, wc));
+                if (ok) {
+                    tc_fence_after();
+                    float o[kN];
+                    tmem_ld16(tmem + lane_base + kColO, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int h = 0; h < kN; ++h) o[h] *= alpha[h];
+                    tmem_st16(tmem + lane_base + kColO, o);
+                    tmem_wait_st();
+                }
+            }
+            // P buffer sb was last read by O of tile j - 2
+            if (ok && j >= 2)
+                ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * sb,
+                                                       ((j - 2) >> 1) & 1, wc));
+            if (ok) {
+                uint8_t* pb = smem + kPOff + (uint32_t)sb * 2u * kOpBytes;
+#pragma unroll
+                for (int h = 0; h < kN; ++h) {
+                    if (h < G) {
+                        const __half hi = __float2half_rn(p[h]);
+                        const __half lo = __float2half_rn(p[h] - __half2float(hi));
+                        const uint32_t off = op_offset(h, tid);
+                        *reinterpret_cast<__half*>(pb + off) = hi;
+                        *reinterpret_cast<__half*>(pb + kOpBytes + off) = lo;
+                    }
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            named_sync_softmax();
+            if (ok && tid == 0) mbar_arrive_local(mb + kBarPFull + 8 * sb);
+        }
+        // Epilogue: this item's (m, l, context) for the G heads.
+        if (ok && n_tiles > 0)
+            ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * ((n_tiles - 1) & 1),
+                                                   ((n_tiles - 1) >> 1) & 1, wc));
+        if (lane == 0) {
+#pragma unroll
+            for (int h = 0; h < kN; ++h) red_sum[warp * kN + h] = l_w[h];
+        }
+        named_sync_softmax();
+        float o[kN];
+        const bool have = ok && n_tiles > 0;
+        if (have) {
+            tc_fence_after();
+            tmem_ld16(tmem + lane_base + kColO, o);
+            tmem_wait_ld();
+        }
+        const int64_t row0 = (int64_t)blockIdx.x * Hq + (int64_t)g * G;
+#pragma unroll
+        for (int h = 0; h < kN; ++h) {
+            if (h < G) {
+                ws.part_ctx[(row0 + h) * kD + tid] = have ? o[h] : 0.f;   // tid = dimension
+                if (tid == h) {
+                    const float l = red_sum[h] + red_sum[kN + h] + red_sum[2 * kN + h] +
+                                    red_sum[3 * kN + h];
+                    ws.part_m[row0 + h] = (have && m_use[h] != -INFINITY) ? m_use[h] * kLn2
+                                                                          : -INFINITY;
+                    ws.part_l[row0 + h] = have ? l : 0.f;
+                }
+            }
+        }
+    }
+
+    // Teardown: every role is done with shared and tensor memory.
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 4) tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace fkv
+
+bool fullkv_tc_supported(const plkv_fullkv_decode_args& a) {
+    return a.head_dim == fkv::kD && a.q_heads % a.kv_heads == 0 &&
+           a.q_heads / a.kv_heads <= fkv::kN && !a.scores && !a.probs;
+}
+
+cudaError_t launch_fullkv_partial_tc(const plkv_fullkv_decode_args& a, DecodeWorkspace ws,
+                                     cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(ws.ctl, 0, kCtlBytes, st);  // the launch's abort word
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fkv::fullkv_partial_tc_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fkv::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    dim3 grid(a.n_items, a.kv_heads);
+    fkv::fullkv_partial_tc_kernel<<<grid, fkv::kThreads, fkv::kSmemBytes, st>>>(
+        a.q, a.k_cache, a.v_cache, a.num_physical, a.kv_heads, a.block_size, a.q_heads,
+        a.scale * 1.4426950408889634f, a.block_tables, a.max_blocks, a.seq_lens, a.items, ws,
+        a.err_flags);
+    return cudaGetLastError();
+}
+
+}  // namespace plkv
