@@ -1116,21 +1116,39 @@ def run_kernel_suite(args) -> dict:
 
     reps = max(1, args.suite_reps)
 
-    def timed(name, kernels, fn, nbytes, note=""):
+    def timed(name, kernels, fn, nbytes, note="", per_call=1):
+        """Device time per call: `reps` calls recorded into a CUDA graph and
+        replayed (launched from Python, calls of a few microseconds would
+        time the host); eager when the call cannot be captured."""
         for _ in range(min(2, reps)):
             fn()
         torch.cuda.synchronize(dev)
+        graph, how = None, "graph"
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize(dev)
+        except Exception:
+            graph, how = None, "eager"
+            torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(reps):
-            fn()
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(reps):
+                fn()
         e1.record()
         torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / reps
+        ms = e0.elapsed_time(e1) / reps / per_call
         gbs = nbytes / (ms * 1e-3) / 1e9
         results.append({"op": name, "kernels": kernels, "us": round(ms * 1e3, 2),
                         "algorithmic_bytes": int(nbytes), "GB/s": round(gbs, 1),
-                        "frac_of_hbm": round(gbs / hbm, 3), "note": note})
+                        "frac_of_hbm": round(gbs / hbm, 3), "timing": how, "note": note})
+        del graph
 
     # FP32 -> FP16 storage conversion
     x = randn(64 << 20)
@@ -1172,7 +1190,7 @@ def run_kernel_suite(args) -> dict:
           ["q_prep_kernel", "latent_partial_tc_kernel"],
           lambda: ops.latent_decode(q_lat, cache, t2, l2, plan, phase="partial", **kw),
           tok * L * 2 + 2 * 128 * L * 4 + 2 * 2048 * 4)
-    timed("latent decode, combine + W_uv (2 sequences)", ["combine_project_kernel"],
+    timed("latent decode, combine + W_uv (2 sequences)", ["merge_rows_kernel", "project_rows_kernel"],
           lambda: ops.latent_decode(q_lat, cache, t2, l2, plan, phase="combine", **kw),
           plan.n_items * 128 * (512 + 2) * 4 + w_uv.numel() * 4 + 2 * 128 * 128 * 4)
     del cache, ws
@@ -1195,7 +1213,7 @@ def run_kernel_suite(args) -> dict:
     timed("latent decode, exact partial pass (64 x 4096 tokens, GQA)", ["latent_partial_exact_kernel"],
           lambda: ops.latent_decode(qlat_buf, cache, tables, lens, plan, phase="partial", **kw),
           B * n_tok * Lg * 2 + B * Hq * Lg * 4, "FP32 CUDA-core bound (64 FLOP/byte)")
-    timed("latent decode, exact combine + W_v", ["combine_project_kernel"],
+    timed("latent decode, exact combine + W_v", ["merge_rows_kernel", "project_rows_kernel"],
           lambda: ops.latent_decode(qlat_buf, cache, tables, lens, plan, phase="combine", **kw),
           plan.n_items * Hq * (Lg + 2) * 4 + w_v.numel() * 4 + ctx.numel() * 4)
     # materialised reconstruction of every active token's K / V, then the full-KV decode
@@ -1213,7 +1231,7 @@ def run_kernel_suite(args) -> dict:
     fws = torch.empty(int(ops.lib().plkv_fullkv_decode_workspace_size(plan.n_items, B, Hq, D)),
                       dtype=torch.uint8, device=dev)
     timed("full-KV decode (64 x 4096 tokens, 8 KV heads, FP16)",
-          ["fullkv_partial_exact_kernel", "combine_project_kernel"],
+          ["fullkv_partial_tc_kernel", "merge_rows_kernel"],
           lambda: ops.fullkv_decode(qg, k16, v16, tables, lens, plan, scale=1 / math.sqrt(D),
                                     out=ctx, workspace=fws),
           B * n_tok * KV * D * 2 * 2 + qg.numel() * 4 + ctx.numel() * 4)
@@ -1264,6 +1282,47 @@ def run_kernel_suite(args) -> dict:
     timed("peer exchange: 2 publishes + 2 merges (1024 rows x 128)",
           ["publish_kernel", "merge_kernel"], peer_step, 2 * (1024 * 129 * 4) * 3,
           "one GPU standing in for two ranks")
+    for e in exch:
+        e.close()
+    del exch, _bufs
+    # Split-K at 8 GPUs, one rank's share of the long-context step (8 x 16384
+    # tokens), with one GPU standing in for the 8 ranks: partial pass, the
+    # head-sharded publish of one rank, and the per-rank cost of publish +
+    # merge + W_uv of 16 heads (all 8 stand-in ranks' calls / 8).
+    W = 8
+    tables, lens_h, lens, P = paged(8, 131072 // W, 64, L, 5)
+    cache = (randn(P, 64, L, scale=0.5)).half()
+    q8 = randn(8, 128, L)
+    plan = ops.plan_workers(lens_h, 64, device=dev)
+    ws = torch.empty(ops.latent_workspace_bytes(plan.n_items, 8, 128, L, 512), dtype=torch.uint8,
+                     device=dev)
+    ctx8 = torch.empty((8, 128, 128), **f32)
+    kw = dict(scale=s.scale, value_dim=512, w_v=w_uv, mode="tc", out=ctx8, workspace=ws,
+              want_lse=True, allow_empty=True)
+    tok8 = 8 * (131072 // W)
+    timed("split-K rank share at 8 GPUs: tensor-core partial pass (8 x 16384 tokens)",
+          ["q_prep_kernel", "latent_partial_tc_kernel"],
+          lambda: ops.latent_decode(q8, cache, tables, lens, plan, phase="partial", **kw),
+          tok8 * L * 2 + 8 * 128 * L * 4)
+    rr = ops.latent_decode(q8, cache, tables, lens, plan, phase="partial", **kw)
+    sx, _sb = mg.ShardExchange.local_group(W, 8, 128, 512, dev)
+    so = torch.empty((8, 128 // W, 128), **f32)
+    item_bytes = plan.n_items * 128 * (512 + 2) * 4
+    timed("split-K at 8 GPUs: head-sharded publish of one rank (8 x 128 rows)",
+          ["shard_publish_kernel"], lambda: sx[0].publish(rr["args"]),
+          item_bytes + 8 * 128 * 516 * 4, "one GPU standing in for the ranks")
+
+    def shard_step():
+        for e in sx:
+            e.publish(rr["args"])
+        for e in sx:
+            e.merge(so, w_v=w_uv)
+    timed("split-K at 8 GPUs: publish + merge + W_uv of 16 heads, per rank",
+          ["shard_publish_kernel", "shard_merge_rows_kernel", "project_rows_kernel"], shard_step,
+          item_bytes + 2 * 8 * 128 * 516 * 4 + w_uv.numel() * 4 // W,
+          "one GPU standing in for the 8 ranks (no NVLink): all ranks' calls / 8", per_call=W)
+    for e in sx:
+        e.close()
     return {"kernel_suite": results, "peak_GB/s": hbm, "peak_source": f"{peak_kind} hbm_gbs"}
 
 def main():

@@ -398,7 +398,12 @@ size_t plkv_fullkv_decode_workspace_size(int32_t n_items, int32_t batch, int32_t
  * paged_full_kv_gqa_decode_fp16_storage_runtime_f32_accum (lib.rs:1147-1269)
  * and paged_gqa_decode_attention_intermediates_ref (attention_ref.py:172-224)
  * on FP16 storage, batched with a table and a length per sequence.  The K and
- * V caches must be 16-byte aligned (PLKV_ERR_UNSUPPORTED otherwise). */
+ * V caches must be 16-byte aligned (PLKV_ERR_UNSUPPORTED otherwise).
+ * head_dim 128 with up to 16 query heads per KV head and no intermediates
+ * (scores / probs NULL) runs on the tensor cores with FP32-accurate
+ * arithmetic (the FP32 query and probabilities split into two FP16 parts);
+ * other shapes (head_dim <= 256, a multiple of 8, up to 8 query heads per KV
+ * head) and calls that want intermediates run on the CUDA cores. */
 int plkv_fullkv_decode(const plkv_fullkv_decode_args* args, plkv_stream_t stream);
 
 /* ------------------------------------------------------------ diagnostics */

@@ -423,7 +423,10 @@ int plkv_fullkv_decode(const plkv_fullkv_decode_args* a, plkv_stream_t stream) {
         return PLKV_ERR_INVALID_ARGUMENT;
     if ((a->scores || a->probs) && a->max_seq_len <= 0) return PLKV_ERR_ZERO_VALUE;
     if (a->probs && !a->scores) return PLKV_ERR_INVALID_ARGUMENT;
-    if (a->head_dim % 8 || a->head_dim > 256 || a->q_heads / a->kv_heads > 8)
+    // the CUDA-core pass takes up to 8 query heads per KV head, the
+    // tensor-core pass (head_dim 128, no intermediates) up to 16
+    if (a->head_dim % 8 || a->head_dim > 256 ||
+        (a->q_heads / a->kv_heads > 8 && !fullkv_tc_supported(*a)))
         return PLKV_ERR_UNSUPPORTED;
     if ((reinterpret_cast<uintptr_t>(a->k_cache) | reinterpret_cast<uintptr_t>(a->v_cache)) & 15)
         return PLKV_ERR_UNSUPPORTED;  // rows are copied in 16-byte pieces

@@ -57,8 +57,8 @@ constexpr uint32_t kKVOff = 0;
 constexpr uint32_t kQOff = kKVOff + kStages * kStageBytes;  // Q hi, Q lo
 constexpr uint32_t kPOff = kQOff + 2 * kOpBytes;            // [2 buffers][hi, lo]
 constexpr uint32_t kMiscOff = kPOff + 4 * kOpBytes;
-constexpr uint32_t kMiscBytes = 1024;
-constexpr uint32_t kSmemBytes = kMiscOff + kMiscBytes;      // 222208
+constexpr uint32_t kMiscBytes = 4096;
+constexpr uint32_t kSmemBytes = kMiscOff + kMiscBytes;      // 225280
 constexpr uint32_t kTmemCols = 64;
 constexpr uint32_t kColS = 0;    // S^T buffers at columns 0 and 16
 constexpr uint32_t kColO = 32;   // O^T
@@ -77,9 +77,10 @@ enum : uint32_t {
     kAbort = kTmemSlot + 4,
     kRedMax = 256,                           // [4 warps][16] float
     kRedSum = kRedMax + 256,                 // [4 warps][16] float
+    kRowSrc = kRedSum + 256,                 // [kStages][kTok] int64 pool offsets of the rows
 };
 static_assert(kAbort + 4 <= kRedMax, "barriers");
-static_assert(kRedSum + 256 <= kMiscBytes, "misc region");
+static_assert(kRowSrc + kStages * kTok * 8 <= kMiscBytes, "misc region");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
@@ -243,28 +244,43 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
         const int li = tid - 160;
         const int chunk = li & 15, rsub = li >> 4;   // 16-byte chunk of a row; row phase
         const int cb = chunk >> 3, cc = chunk & 7;
+        // Loader warp lw covers the rows r = 4k + 2 lw + {0, 1} of every tile.
+        // Its lanes first resolve those 64 rows' pool offsets (two table
+        // loads per lane, in flight together) into shared memory, then copy
+        // the rows: one table round trip per tile instead of one per row.
+        const int lw = li >> 5, ln = li & 31;
+        int64_t* rowsrc = reinterpret_cast<int64_t*>(misc + kRowSrc);   // [kStages][kTok]
         auto issue = [&](int j) {
-            const uint32_t kdst = sbase + kKVOff + (uint32_t)(j % kStages) * kStageBytes;
+            const int st = j % kStages;
+            const uint32_t kdst = sbase + kKVOff + (uint32_t)st * kStageBytes;
             const uint32_t vdst = kdst + kTileBytes;
             const int t0 = t_begin + j * kTok;
-#pragma unroll 4
-            for (int k = 0; k < kTok / 4; ++k) {
-                const int r = rsub + 4 * k;
+            int64_t* rs = rowsrc + st * kTok;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int r = 4 * ln + 2 * lw + e;
                 const int t = t0 + r;
-                const uint32_t off = (uint32_t)cb * kHalf + (uint32_t)(r >> 3) * 1024u +
-                                     (uint32_t)(r & 7) * 128u +
-                                     (((uint32_t)cc ^ (uint32_t)(r & 7)) << 4);
                 int64_t src = -1;
                 if (t < t_end) {
                     const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
                     if (phys >= 0 && phys < num_physical)
-                        src = (((int64_t)phys * KV + g) * bs + (t % bs)) * kD + chunk * 8;
-                    else if (g == 0 && chunk == 0)
+                        src = (((int64_t)phys * KV + g) * bs + (t % bs)) * kD;
+                    else if (g == 0)
                         set_flag(flags, PLKV_FLAG_BAD_BLOCK);
                 }
+                rs[r] = src;
+            }
+            __syncwarp();
+#pragma unroll 8
+            for (int k = 0; k < kTok / 4; ++k) {
+                const int r = rsub + 4 * k;
+                const uint32_t off = (uint32_t)cb * kHalf + (uint32_t)(r >> 3) * 1024u +
+                                     (uint32_t)(r & 7) * 128u +
+                                     (((uint32_t)cc ^ (uint32_t)(r & 7)) << 4);
+                const int64_t src = rs[r];
                 if (src >= 0) {
-                    cp_async16(kdst + off, k_cache + src);
-                    cp_async16(vdst + off, v_cache + src);
+                    cp_async16(kdst + off, k_cache + src + chunk * 8);
+                    cp_async16(vdst + off, v_cache + src + chunk * 8);
                 } else {
                     st_shared_zero16(kdst + off);
                     st_shared_zero16(vdst + off);
@@ -285,8 +301,9 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
             if (jn < n_tiles) {
                 // the stage held tile jn - kStages, read by its S and O
                 if (jn >= kStages &&
-                    !(ok = mbar_wait(mb + kBarKVEmpty + 8 * (jn % kStages),
-                                     ((jn / kStages) - 1) & 1, wc)))
+                    !(ok = __all_sync(0xffffffffu,
+                                      mbar_wait(mb + kBarKVEmpty + 8 * (jn % kStages),
+                                                ((jn / kStages) - 1) & 1, wc))))
                     break;
                 issue(jn);
             } else {
