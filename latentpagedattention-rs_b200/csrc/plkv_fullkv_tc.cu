@@ -218,14 +218,26 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
         fence_mbar_init();
     }
     // Q^T as high and low FP16 parts (rows >= G zero), both P buffers zero.
-    for (int i = tid; i < kN * kD; i += kThreads) {
-        const int h = i / kD, d = i - h * kD;
-        const float x = h < G ? q[((int64_t)b * Hq + g * G + h) * kD + d] : 0.f;
-        const __half hi = __float2half_rn(x);
-        const __half lo = __float2half_rn(x - __half2float(hi));
-        const uint32_t off = op_offset(h, d);
-        *reinterpret_cast<__half*>(smem + kQOff + off) = hi;
-        *reinterpret_cast<__half*>(smem + kQOff + kOpBytes + off) = lo;
+    {
+        // all of this thread's query loads in flight together
+        constexpr int kPer = (kN * kD + kThreads - 1) / kThreads;
+        float qv[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int i = tid + u * kThreads, h = i / kD, d = i - h * kD;
+            qv[u] = (i < kN * kD && h < G) ? q[((int64_t)b * Hq + g * G + h) * kD + d] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int i = tid + u * kThreads, h = i / kD, d = i - h * kD;
+            if (i < kN * kD) {
+                const __half hi = __float2half_rn(qv[u]);
+                const __half lo = __float2half_rn(qv[u] - __half2float(hi));
+                const uint32_t off = op_offset(h, d);
+                *reinterpret_cast<__half*>(smem + kQOff + off) = hi;
+                *reinterpret_cast<__half*>(smem + kQOff + kOpBytes + off) = lo;
+            }
+        }
     }
     for (int i = tid; i < (int)(4 * kOpBytes / 16); i += kThreads)
         reinterpret_cast<uint4*>(smem + kPOff)[i] = make_uint4(0, 0, 0, 0);
@@ -250,27 +262,33 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
         // the rows: one table round trip per tile instead of one per row.
         const int lw = li >> 5, ln = li & 31;
         int64_t* rowsrc = reinterpret_cast<int64_t*>(misc + kRowSrc);   // [kStages][kTok]
-        auto issue = [&](int j) {
-            const int st = j % kStages;
-            const uint32_t kdst = sbase + kKVOff + (uint32_t)st * kStageBytes;
-            const uint32_t vdst = kdst + kTileBytes;
+        // rows of tile j: pool offsets into rowsrc[j % kStages]
+        auto resolve = [&](int j) {
+            if (j >= n_tiles) return;
+            int64_t* rs = rowsrc + (j % kStages) * kTok;
             const int t0 = t_begin + j * kTok;
-            int64_t* rs = rowsrc + st * kTok;
+            int64_t src[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                const int r = 4 * ln + 2 * lw + e;
-                const int t = t0 + r;
-                int64_t src = -1;
+                const int t = t0 + 4 * ln + 2 * lw + e;
+                src[e] = -1;
                 if (t < t_end) {
                     const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
                     if (phys >= 0 && phys < num_physical)
-                        src = (((int64_t)phys * KV + g) * bs + (t % bs)) * kD;
+                        src[e] = (((int64_t)phys * KV + g) * bs + (t % bs)) * kD;
                     else if (g == 0)
                         set_flag(flags, PLKV_FLAG_BAD_BLOCK);
                 }
-                rs[r] = src;
             }
-            __syncwarp();
+            rs[4 * ln + 2 * lw] = src[0];
+            rs[4 * ln + 2 * lw + 1] = src[1];
+        };
+        // copies of tile j (rows resolved before), one commit group
+        auto copy = [&](int j) {
+            const int st = j % kStages;
+            const uint32_t kdst = sbase + kKVOff + (uint32_t)st * kStageBytes;
+            const uint32_t vdst = kdst + kTileBytes;
+            const int64_t* rs = rowsrc + st * kTok;
 #pragma unroll 8
             for (int k = 0; k < kTok / 4; ++k) {
                 const int r = rsub + 4 * k;
@@ -289,8 +307,10 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
             cp_async_commit();
         };
         bool ok = true;
+        for (int j = 0; j < kStages; ++j) resolve(j);
+        __syncwarp();
         for (int j = 0; j < kStages - 1; ++j) {
-            if (j < n_tiles) issue(j);
+            if (j < n_tiles) copy(j);
             else cp_async_commit();
         }
         for (int j = 0; ok && j < n_tiles; ++j) {
@@ -305,10 +325,14 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
                                       mbar_wait(mb + kBarKVEmpty + 8 * (jn % kStages),
                                                 ((jn / kStages) - 1) & 1, wc))))
                     break;
-                issue(jn);
+                copy(jn);
             } else {
                 cp_async_commit();
             }
+            // rows of tile j + kStages into the slot copy(j) read, while the
+            // copies in flight land
+            resolve(j + kStages);
+            __syncwarp();
         }
         cp_async_wait<0>();
     } else if (warp == 4) {
@@ -316,12 +340,10 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
         if (lane == 0 && n_tiles > 0) {
             const uint32_t id_s = idesc_f16(128, kN, false, false);
             const uint32_t id_o = idesc_f16(128, kN, true, false);
-            auto issue_s = [&](int j) -> bool {
+            // S of tile j (its K landed; S buffer j & 1 read by the softmax
+            // of tile j - 2)
+            auto issue_s = [&](int j) {
                 const int st = j % kStages, sb = j & 1;
-                if (!mbar_wait(mb + kBarKVFull + 8 * st, (j / kStages) & 1, wc)) return false;
-                // S buffer sb was last read by the softmax of tile j - 2
-                if (j >= 2 && !mbar_wait(mb + kBarPFull + 8 * sb, ((j - 2) >> 1) & 1, wc))
-                    return false;
                 tc_fence_after();
                 const uint32_t kt = sbase + kKVOff + (uint32_t)st * kStageBytes;
 #pragma unroll
@@ -335,11 +357,10 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
                             sdesc_sw128(sbase + kQOff + kOpBytes + qoff, 16, 1024), id_s, 1u);
                 }
                 mma_commit(mb + kBarSFull + 8 * sb);
-                return true;
             };
-            auto issue_o = [&](int j) -> bool {
+            // O of tile j (its P written)
+            auto issue_o = [&](int j) {
                 const int st = j % kStages, pb = j & 1;
-                if (!mbar_wait(mb + kBarPFull + 8 * pb, (j >> 1) & 1, wc)) return false;
                 tc_fence_after();
                 const uint32_t vt = sbase + kKVOff + (uint32_t)st * kStageBytes + kTileBytes;
                 const uint32_t pbase = sbase + kPOff + (uint32_t)pb * 2u * kOpBytes;
@@ -355,12 +376,48 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
                 }
                 mma_commit(mb + kBarODone + 8 * pb);
                 mma_commit(mb + kBarKVEmpty + 8 * st);
-                return true;
             };
-            bool ok = issue_s(0);
-            for (int j = 0; ok && j < n_tiles; ++j) {
-                if (j + 1 < n_tiles) ok = issue_s(j + 1);
-                if (ok) ok = issue_o(j);
+            // Non-blocking: the S of the next tile as soon as its K and V
+            // landed and its S buffer is free, the O of a tile as soon as its
+            // P is written, whichever comes first; waits polled with
+            // test_wait, bounded as in mbar_wait.
+            int sj = 0, oj = 0;
+            uint64_t idle_since = 0, next_check = 0;
+            while (oj < n_tiles) {
+                bool did = false;
+                if (sj < n_tiles &&
+                    mbar_test_wait(mb + kBarKVFull + 8 * (sj % kStages), (sj / kStages) & 1) &&
+                    (sj < 2 || mbar_test_wait(mb + kBarPFull + 8 * (sj & 1), ((sj - 2) >> 1) & 1))) {
+                    issue_s(sj);
+                    ++sj;
+                    did = true;
+                }
+                if (oj < sj && mbar_test_wait(mb + kBarPFull + 8 * (oj & 1), (oj >> 1) & 1)) {
+                    issue_o(oj);
+                    ++oj;
+                    did = true;
+                }
+                if (did) {
+                    idle_since = 0;
+                } else if (*abort_flag) {
+                    break;
+                } else {
+                    const uint64_t now = globaltimer();
+                    if (idle_since == 0) {
+                        idle_since = now;
+                        next_check = now + kFlagPollNs;
+                    } else if (now >= next_check) {
+                        next_check = now + kFlagPollNs;
+                        if (*wc.abort) {
+                            *abort_flag = 1;
+                            break;
+                        }
+                        if (now - idle_since > kWaitLimitNs) {
+                            wait_give_up(wc);
+                            break;
+                        }
+                    }
+                }
             }
         }
         __syncwarp();
