@@ -19,15 +19,21 @@
 // twice; FP16 x FP16 products are exact in FP32, so scores and context carry
 // FP32 accumulation error only (~1e-7 relative; the exact-mode bar is 1e-5).
 //
-// Data movement: the K and V rows of a tile are gathered by two loader warps
-// with 16-byte cp.async copies straight into the 128-byte-swizzled operand
-// layouts (K: K-major [2 column blocks][128 rows][128 B]; V is the same bytes
-// read as the MN-major A operand V^T), three 64 KiB stages in flight.  Rows
-// of a block are 256 contiguous bytes of the head-major pool, so a warp copies
-// two rows = 512 contiguous bytes per instruction; blocks of 16 rows would
-// need 16 TMA boxes per tile and operand.  Rows past the item's end, or of a
-// table entry outside the pool, are zeroed instead (0 x garbage must stay 0 in
-// the context MMA).
+// Data movement: one TMA box per 16 tokens of a block and operand.  A block of
+// KV head g is 16 rows x 256 contiguous bytes of the head-major pool (more
+// for larger blocks), so the pool is viewed as a 4-D tensor (64 columns, 8
+// rows, 2 column halves, 8-row groups): a box of 2 groups lands as
+// [group][half][8 rows][128 B] with the 128-byte swizzle, and the 8 chunks of
+// a 128-token tile laid side by side put the 8-row groups of each 64-column
+// half at a uniform 2 KiB stride -- the SW128 K-major operand layout of K
+// (column block h at h x 1 KiB, SBO 2 KiB) and, read as the MN-major A
+// operand of O^T, of V (LBO 1 KiB between the halves, SBO 2 KiB).  16 boxes of
+// 4 KiB per tile, three 64 KiB stages in flight, issued by one thread (16-byte
+// copies from the SM's load-store path reached only ~18 GB/s per SM: too few
+// requests in flight).  Chunks past the item's end, or of a table entry outside
+// the pool, are read at an out-of-bounds group index and arrive as zeros; the
+// rows past the end inside the item's last chunk are zeroed by the softmax
+// warps before they release P (0 x garbage must stay 0 in the context MMA).
 //
 // Softmax: TMEM lane = token; per head a warp-shuffle max over the lanes and
 // the four warps through shared memory; log2 domain with a lazily updated
@@ -35,13 +41,19 @@
 // only when a head's max moved by more than that.
 //
 // Warps: 0-3 softmax and epilogue, 4 tensor-memory allocation and (lane 0)
-// MMA issue, 5-6 loaders.  Every wait is bounded (1 s): on expiry the kernel
+// MMA issue, 5 loads.  Every wait is bounded (1 s): on expiry the kernel
 // records PLKV_FLAG_TIMEOUT, abandons its work and frees tensor memory.
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
 #include "plkv_sm100.cuh"
 
 namespace plkv {
+namespace tc {
+bool encode_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank,
+                const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+                CUtensorMapSwizzle swizzle);
+}
 namespace fkv {
 
 constexpr int kTok = 128;        // tokens per tile
@@ -57,18 +69,19 @@ constexpr uint32_t kKVOff = 0;
 constexpr uint32_t kQOff = kKVOff + kStages * kStageBytes;  // Q hi, Q lo
 constexpr uint32_t kPOff = kQOff + 2 * kOpBytes;            // [2 buffers][hi, lo]
 constexpr uint32_t kMiscOff = kPOff + 4 * kOpBytes;
-constexpr uint32_t kMiscBytes = 4096;
-constexpr uint32_t kSmemBytes = kMiscOff + kMiscBytes;      // 225280
+constexpr uint32_t kMiscBytes = 1024;
+constexpr uint32_t kSmemBytes = kMiscOff + kMiscBytes;      // 222208
 constexpr uint32_t kTmemCols = 64;
 constexpr uint32_t kColS = 0;    // S^T buffers at columns 0 and 16
 constexpr uint32_t kColO = 32;   // O^T
-constexpr int kLoaders = 64;
-constexpr int kThreads = 224;
+constexpr int kThreads = 192;
+constexpr int kChunks = kTok / 16;                 // 16-token TMA boxes per tile and operand
+constexpr uint32_t kChunkBytes = 16 * 256;         // one box: 2 groups x 2 halves x 8 rows x 128 B
 constexpr float kTau = 8.f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 enum : uint32_t {
-    kBarKVFull = 0,                          // [kStages] loaders: the tile's K and V landed
+    kBarKVFull = 0,                          // [kStages] TMA: the tile's K and V landed
     kBarKVEmpty = kBarKVFull + 8 * kStages,  // [kStages] MMA commit: S and O of the tile done
     kBarSFull = kBarKVEmpty + 8 * kStages,   // [2] MMA commit: S^T of the tile in TMEM
     kBarPFull = kBarSFull + 16,              // [2] softmax: P of the tile written
@@ -77,10 +90,9 @@ enum : uint32_t {
     kAbort = kTmemSlot + 4,
     kRedMax = 256,                           // [4 warps][16] float
     kRedSum = kRedMax + 256,                 // [4 warps][16] float
-    kRowSrc = kRedSum + 256,                 // [kStages][kTok] int64 pool offsets of the rows
 };
 static_assert(kAbort + 4 <= kRedMax, "barriers");
-static_assert(kRowSrc + kStages * kTok * 8 <= kMiscBytes, "misc region");
+static_assert(kRedSum + 256 <= kMiscBytes, "misc region");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
@@ -138,18 +150,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
         : "memory");
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void st_shared_zero16(uint32_t dst) {
-    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+// A 16-token box (2 x 8 rows, both 64-column halves) of the 4-D pool view at
+// 8-row group index `grp`; completes on `bar` of this CTA.
+__device__ __forceinline__ void tma_chunk(uint32_t dst, const CUtensorMap* map, int grp,
+                                          uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(0), "r"(grp),
+          "r"(bar), "l"(policy)
+        : "memory");
 }
 
 __device__ __forceinline__ void named_sync_softmax() {
@@ -172,8 +182,9 @@ __device__ __forceinline__ uint32_t op_offset(int row, int k) {
 
 // grid = (n_items, KV heads), block = 224, one CTA per SM (222 KiB).
 __global__ void __launch_bounds__(kThreads, 1)
-fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict__ k_cache,
-                         const uint16_t* __restrict__ v_cache, int64_t num_physical, int KV,
+fullkv_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
+                         const __grid_constant__ CUtensorMap v_map, int64_t n_groups,
+                         const float* __restrict__ q, int64_t num_physical, int KV,
                          int bs, int Hq, float scale_log2, const int32_t* __restrict__ tables,
                          int64_t max_blocks, const int32_t* __restrict__ seq_lens,
                          const plkv_work_item* __restrict__ items, DecodeWorkspace ws,
@@ -206,7 +217,7 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(mb + kBarKVFull + 8 * s, kLoaders);
+            mbar_init(mb + kBarKVFull + 8 * s, 1);
             mbar_init(mb + kBarKVEmpty + 8 * s, 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -251,90 +262,47 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(misc + kTmemSlot);
 
-    if (warp >= 5) {
-        // ------------------------------------------------------------ loaders
-        const int li = tid - 160;
-        const int chunk = li & 15, rsub = li >> 4;   // 16-byte chunk of a row; row phase
-        const int cb = chunk >> 3, cc = chunk & 7;
-        // Loader warp lw covers the rows r = 4k + 2 lw + {0, 1} of every tile.
-        // Its lanes first resolve those 64 rows' pool offsets (two table
-        // loads per lane, in flight together) into shared memory, then copy
-        // the rows: one table round trip per tile instead of one per row.
-        const int lw = li >> 5, ln = li & 31;
-        int64_t* rowsrc = reinterpret_cast<int64_t*>(misc + kRowSrc);   // [kStages][kTok]
-        // rows of tile j: pool offsets into rowsrc[j % kStages]
-        auto resolve = [&](int j) {
-            if (j >= n_tiles) return;
-            int64_t* rs = rowsrc + (j % kStages) * kTok;
-            const int t0 = t_begin + j * kTok;
-            int64_t src[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int t = t0 + 4 * ln + 2 * lw + e;
-                src[e] = -1;
-                if (t < t_end) {
-                    const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
-                    if (phys >= 0 && phys < num_physical)
-                        src[e] = (((int64_t)phys * KV + g) * bs + (t % bs)) * kD;
-                    else if (g == 0)
-                        set_flag(flags, PLKV_FLAG_BAD_BLOCK);
-                }
+    if (warp == 5) {
+        // -------------------------------------------------------------- loads
+        // Lane c < 8 resolves chunk c of a tile (its 8-row group index, or an
+        // out-of-bounds index past the item or for a table entry outside the
+        // pool) before the wait for the stage; lane 0 then issues the 16 boxes.
+        const uint64_t pol = policy_evict_first();
+        auto group_of = [&](int j) -> int {
+            const int t = t_begin + j * kTok + 16 * lane;
+            int grp = (int)n_groups;   // out of bounds: zeros
+            if (lane < kChunks && t < t_end) {
+                const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
+                if (phys >= 0 && phys < num_physical)
+                    grp = (int)((((int64_t)phys * KV + g) * bs + (t % bs)) >> 3);
+                else if (g == 0)
+                    set_flag(flags, PLKV_FLAG_BAD_BLOCK);
             }
-            rs[4 * ln + 2 * lw] = src[0];
-            rs[4 * ln + 2 * lw + 1] = src[1];
-        };
-        // copies of tile j (rows resolved before), one commit group
-        auto copy = [&](int j) {
-            const int st = j % kStages;
-            const uint32_t kdst = sbase + kKVOff + (uint32_t)st * kStageBytes;
-            const uint32_t vdst = kdst + kTileBytes;
-            const int64_t* rs = rowsrc + st * kTok;
-#pragma unroll 8
-            for (int k = 0; k < kTok / 4; ++k) {
-                const int r = rsub + 4 * k;
-                const uint32_t off = (uint32_t)cb * kHalf + (uint32_t)(r >> 3) * 1024u +
-                                     (uint32_t)(r & 7) * 128u +
-                                     (((uint32_t)cc ^ (uint32_t)(r & 7)) << 4);
-                const int64_t src = rs[r];
-                if (src >= 0) {
-                    cp_async16(kdst + off, k_cache + src + chunk * 8);
-                    cp_async16(vdst + off, v_cache + src + chunk * 8);
-                } else {
-                    st_shared_zero16(kdst + off);
-                    st_shared_zero16(vdst + off);
-                }
-            }
-            cp_async_commit();
+            return grp;
         };
         bool ok = true;
-        for (int j = 0; j < kStages; ++j) resolve(j);
-        __syncwarp();
-        for (int j = 0; j < kStages - 1; ++j) {
-            if (j < n_tiles) copy(j);
-            else cp_async_commit();
-        }
         for (int j = 0; ok && j < n_tiles; ++j) {
-            cp_async_wait<kStages - 2>();   // this thread's copies of tile j landed
-            fence_proxy_async_smem();       // ... and are visible to the tensor core
-            mbar_arrive_local(mb + kBarKVFull + 8 * (j % kStages));
-            const int jn = j + kStages - 1;
-            if (jn < n_tiles) {
-                // the stage held tile jn - kStages, read by its S and O
-                if (jn >= kStages &&
-                    !(ok = __all_sync(0xffffffffu,
-                                      mbar_wait(mb + kBarKVEmpty + 8 * (jn % kStages),
-                                                ((jn / kStages) - 1) & 1, wc))))
-                    break;
-                copy(jn);
-            } else {
-                cp_async_commit();
+            const int grp = group_of(j);
+            const int st = j % kStages;
+            if (j >= kStages)
+                ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarKVEmpty + 8 * st,
+                                                       ((j / kStages) - 1) & 1, wc));
+            if (!ok) break;
+            int grps[kChunks];
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) grps[c] = __shfl_sync(0xffffffffu, grp, c);
+            if (lane == 0) {
+                const uint32_t bar = mb + kBarKVFull + 8 * st;
+                const uint32_t kdst = sbase + kKVOff + (uint32_t)st * kStageBytes;
+                mbar_arrive_expect_tx(bar, kStageBytes);
+#pragma unroll
+                for (int c = 0; c < kChunks; ++c) {
+                    tma_chunk(kdst + c * kChunkBytes, &k_map, grps[c], bar, pol);
+                    tma_chunk(kdst + kTileBytes + c * kChunkBytes, &v_map, grps[c], bar, pol);
+                }
             }
-            // rows of tile j + kStages into the slot copy(j) read, while the
-            // copies in flight land
-            resolve(j + kStages);
             __syncwarp();
         }
-        cp_async_wait<0>();
     } else if (warp == 4) {
         // --------------------------------------------------------- MMA issue
         if (lane == 0 && n_tiles > 0) {
@@ -348,9 +316,9 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
                 const uint32_t kt = sbase + kKVOff + (uint32_t)st * kStageBytes;
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk) {
-                    const uint32_t koff = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
+                    const uint32_t koff = (uint32_t)(kk >> 2) * 1024u + (uint32_t)(kk & 3) * 32u;
                     const uint32_t qoff = (uint32_t)(kk >> 2) * kOpBlock + (uint32_t)(kk & 3) * 32u;
-                    const uint64_t a = sdesc_sw128(kt + koff, 16, 1024);
+                    const uint64_t a = sdesc_sw128(kt + koff, 16, 2048);
                     mma_f16(tmem + kColS + 16 * sb, a, sdesc_sw128(sbase + kQOff + qoff, 16, 1024),
                             id_s, kk > 0 ? 1u : 0u);
                     mma_f16(tmem + kColS + 16 * sb, a,
@@ -366,8 +334,9 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
                 const uint32_t pbase = sbase + kPOff + (uint32_t)pb * 2u * kOpBytes;
 #pragma unroll
                 for (int kt = 0; kt < kTok / 16; ++kt) {
-                    // V^T: MN-major, 64-dim blocks kHalf apart, 8-token groups 1 KiB apart
-                    const uint64_t a = sdesc_sw128(vt + (uint32_t)kt * 2048u, kHalf, 1024);
+                    // V^T: MN-major, the two 64-dim halves 1 KiB apart, 8-token
+                    // groups 2 KiB apart, 16 tokens = one box
+                    const uint64_t a = sdesc_sw128(vt + (uint32_t)kt * kChunkBytes, 1024, 2048);
                     const uint32_t poff = (uint32_t)(kt >> 2) * kOpBlock + (uint32_t)(kt & 3) * 32u;
                     mma_f16(tmem + kColO, a, sdesc_sw128(pbase + poff, 16, 1024), id_o,
                             (j > 0 || kt > 0) ? 1u : 0u);
@@ -519,6 +488,27 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
                     }
                 }
             }
+            // Last tile of the item: the rows past its end inside the last
+            // loaded box hold whatever the pool holds there; zero their V
+            // rows once the tile landed (p = 0 there, and 0 x garbage must
+            // stay 0).  Boxes wholly past the end arrived as zeros.
+            const int nt = min(kTok, t_end - (t_begin + j * kTok));
+            if (ok && (nt & 15) != 0) {
+                const int st = j % kStages;
+                ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarKVFull + 8 * st,
+                                                       (j / kStages) & 1, wc));
+                if (ok) {
+                    uint8_t* vt = smem + kKVOff + (uint32_t)st * kStageBytes + kTileBytes;
+                    const int rows = 16 - (nt & 15);
+                    for (int i = tid; i < rows * 16; i += 128) {
+                        const int r = nt + (i >> 4), h = (i >> 3) & 1, c16 = i & 7;
+                        *reinterpret_cast<uint4*>(vt + (r >> 4) * kChunkBytes +
+                                                  ((r >> 3) & 1) * 2048 + h * 1024 +
+                                                  (r & 7) * 128 + c16 * 16) =
+                            make_uint4(0, 0, 0, 0);
+                    }
+                }
+            }
             fence_proxy_async_smem();
             tc_fence_before();
             named_sync_softmax();
@@ -567,11 +557,24 @@ fullkv_partial_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict
 
 bool fullkv_tc_supported(const plkv_fullkv_decode_args& a) {
     return a.head_dim == fkv::kD && a.q_heads % a.kv_heads == 0 &&
-           a.q_heads / a.kv_heads <= fkv::kN && !a.scores && !a.probs;
+           a.q_heads / a.kv_heads <= fkv::kN && !a.scores && !a.probs && a.block_size % 16 == 0 &&
+           a.num_physical * a.kv_heads * (int64_t)a.block_size / 8 < (1ll << 31);
 }
 
 cudaError_t launch_fullkv_partial_tc(const plkv_fullkv_decode_args& a, DecodeWorkspace ws,
                                      cudaStream_t st) {
+    // 4-D view of a head-major pool [P, KV, bs, 128] FP16: (64 columns, 8 rows,
+    // 2 column halves, 8-row groups), a box = 16 rows of one block
+    const cuuint64_t n_groups = (cuuint64_t)a.num_physical * a.kv_heads * a.block_size / 8;
+    const cuuint64_t dims[4] = {64, 8, 2, n_groups};
+    const cuuint64_t strides[3] = {256, 128, 2048};
+    const cuuint32_t box[4] = {64, 8, 2, 2};
+    CUtensorMap k_map, v_map;
+    if (!tc::encode_map(&k_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.k_cache, 4, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !tc::encode_map(&v_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.v_cache, 4, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
     cudaError_t e = cudaMemsetAsync(ws.ctl, 0, kCtlBytes, st);  // the launch's abort word
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(fkv::fullkv_partial_tc_kernel,
@@ -579,7 +582,7 @@ cudaError_t launch_fullkv_partial_tc(const plkv_fullkv_decode_args& a, DecodeWor
     if (e != cudaSuccess) return e;
     dim3 grid(a.n_items, a.kv_heads);
     fkv::fullkv_partial_tc_kernel<<<grid, fkv::kThreads, fkv::kSmemBytes, st>>>(
-        a.q, a.k_cache, a.v_cache, a.num_physical, a.kv_heads, a.block_size, a.q_heads,
+        k_map, v_map, (int64_t)n_groups, a.q, a.num_physical, a.kv_heads, a.block_size, a.q_heads,
         a.scale * 1.4426950408889634f, a.block_tables, a.max_blocks, a.seq_lens, a.items, ws,
         a.err_flags);
     return cudaGetLastError();
