@@ -90,9 +90,10 @@ enum : uint32_t {
     kAbort = kTmemSlot + 4,
     kRedMax = 256,                           // [4 warps][16] float
     kRedSum = kRedMax + 256,                 // [4 warps][16] float
+    kVote = kRedSum + 256,                   // [4 warps] int: some score above the running max
 };
 static_assert(kAbort + 4 <= kRedMax, "barriers");
-static_assert(kRedSum + 256 <= kMiscBytes, "misc region");
+static_assert(kVote + 16 <= kMiscBytes, "misc region");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 __device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
@@ -395,26 +396,33 @@ fullkv_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
         const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
         float* red_max = reinterpret_cast<float*>(misc + kRedMax);
         float* red_sum = reinterpret_cast<float*>(misc + kRedSum);
-        float m_use[kN], l_w[kN];
+        // m_use: the running max per head (identical in every thread); l_t:
+        // this thread's share of the row sums (its token's probabilities),
+        // reduced over the CTA once, in the epilogue.
+        float m_use[kN], l_t[kN];
 #pragma unroll
         for (int h = 0; h < kN; ++h) {
             m_use[h] = -INFINITY;
-            l_w[h] = 0.f;
+            l_t[h] = 0.f;
         }
+        int* vote = reinterpret_cast<int*>(misc + kVote);
+        // This thread's token of tile j: inside the item and of a block inside
+        // the pool (boxes of any other arrived as zeros); looked up a tile
+        // ahead, so that the table load never stalls the softmax.
+        auto token_ok = [&](int j) -> bool {
+            const int t = t_begin + j * kTok + tid;
+            if (j >= n_tiles || t >= t_end) return false;
+            const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
+            return phys >= 0 && phys < num_physical;
+        };
+        bool tok_next = token_ok(0);
         bool ok = true;
         // Every softmax thread runs every iteration and reaches every named
         // barrier; after a failed wait it only skips the work.
         for (int j = 0; j < n_tiles; ++j) {
             const int sb = j & 1;
-            // This thread's token: inside the item and of a block inside the
-            // pool (the loaders zeroed the rows of any other), looked up
-            // before the wait so that the load overlaps it.
-            const int t = t_begin + j * kTok + tid;
-            bool tok_ok = t < t_end;
-            if (tok_ok) {
-                const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
-                tok_ok = phys >= 0 && phys < num_physical;
-            }
+            const bool tok_ok = tok_next;
+            tok_next = token_ok(j + 1);
             if (ok)
                 ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarSFull + 8 * sb, (j >> 1) & 1, wc));
             float s[kN];
@@ -424,37 +432,52 @@ fullkv_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                 tmem_wait_ld();
             }
             const bool valid = ok && tok_ok;
+            // Lazy running max: the tile's exact max per head is needed only
+            // when some score exceeds the running max by more than kTau
+            // (rare after the first tiles); a CTA-wide vote decides.
+            bool above = false;
 #pragma unroll
             for (int h = 0; h < kN; ++h) {
                 s[h] = (valid && h < G) ? s[h] * scale_log2 : -INFINITY;
-                if (h < G) {
-                    const float mx = warp_max(s[h]);
-                    if (lane == 0) red_max[warp * kN + h] = mx;
-                }
+                above |= s[h] > m_use[h] + kTau;
             }
+            above = __any_sync(0xffffffffu, above);
+            if (lane == 0) vote[warp] = above ? 1 : 0;
             named_sync_softmax();
+            const bool resc = (vote[0] | vote[1] | vote[2] | vote[3]) != 0;
             float alpha[kN];
-            bool resc = false;
 #pragma unroll
-            for (int h = 0; h < kN; ++h) {
-                alpha[h] = 1.f;
-                if (h < G) {
-                    const float mt = fmaxf(fmaxf(red_max[h], red_max[kN + h]),
-                                           fmaxf(red_max[2 * kN + h], red_max[3 * kN + h]));
-                    const float m_new = fmaxf(m_use[h], mt);
-                    if (m_new > m_use[h] + kTau) {
-                        alpha[h] = (m_use[h] == -INFINITY) ? 0.f : fast_exp2(m_use[h] - m_new);
-                        m_use[h] = m_new;
-                        l_w[h] *= alpha[h];
-                        resc = true;
+            for (int h = 0; h < kN; ++h) alpha[h] = 1.f;
+            if (resc) {
+#pragma unroll
+                for (int h = 0; h < kN; ++h) {
+                    if (h < G) {
+                        const float mx = warp_max(s[h]);
+                        if (lane == 0) red_max[warp * kN + h] = mx;
                     }
                 }
+                named_sync_softmax();
+#pragma unroll
+                for (int h = 0; h < kN; ++h) {
+                    if (h < G) {
+                        const float mt = fmaxf(fmaxf(red_max[h], red_max[kN + h]),
+                                               fmaxf(red_max[2 * kN + h], red_max[3 * kN + h]));
+                        const float m_new = fmaxf(m_use[h], mt);
+                        if (m_new > m_use[h]) {
+                            alpha[h] = (m_use[h] == -INFINITY) ? 0.f : fast_exp2(m_use[h] - m_new);
+                            m_use[h] = m_new;
+                            l_t[h] *= alpha[h];
+                        }
+                    }
+                }
+                // the votes and maxima are read; the next tile may write them
+                named_sync_softmax();
             }
             float p[kN];
 #pragma unroll
             for (int h = 0; h < kN; ++h) {
                 p[h] = (h < G && s[h] != -INFINITY) ? fast_exp2(s[h] - m_use[h]) : 0.f;
-                if (h < G) l_w[h] += warp_sum(p[h]);
+                l_t[h] += p[h];
             }
             if (ok && resc && j > 0) {
                 // O^T through tile j - 1 must be complete before it is rescaled
@@ -518,9 +541,12 @@ fullkv_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
         if (ok && n_tiles > 0)
             ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * ((n_tiles - 1) & 1),
                                                    ((n_tiles - 1) >> 1) & 1, wc));
-        if (lane == 0) {
 #pragma unroll
-            for (int h = 0; h < kN; ++h) red_sum[warp * kN + h] = l_w[h];
+        for (int h = 0; h < kN; ++h) {
+            if (h < G) {
+                const float lw = warp_sum(l_t[h]);
+                if (lane == 0) red_sum[warp * kN + h] = lw;
+            }
         }
         named_sync_softmax();
         float o[kN];
