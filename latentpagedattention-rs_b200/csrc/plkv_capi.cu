@@ -25,9 +25,6 @@ cudaError_t launch_latent_partial_exact(const plkv_latent_decode_args&, DecodeWo
 cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args&, DecodeWorkspace,
                                      cudaStream_t);
 bool tc_supported(const plkv_latent_decode_args&);
-cudaError_t launch_latent_partial_tc2(const plkv_latent_decode_args&, DecodeWorkspace,
-                                      cudaStream_t);
-bool tc2_supported(const plkv_latent_decode_args&);
 bool fullkv_tc_supported(const plkv_fullkv_decode_args&);
 cudaError_t launch_fullkv_partial_tc(const plkv_fullkv_decode_args&, DecodeWorkspace,
                                      cudaStream_t);
@@ -316,14 +313,8 @@ int plkv_latent_decode_partial(const plkv_latent_decode_args* a, plkv_stream_t s
                                          a->latent_dim, a->value_dim);
     cudaError_t e;
     if (a->mode == PLKV_MODE_TC_F16) {
-        static const bool v1 = getenv("PLKV_TC_V2") == nullptr;  // A/B of the two passes
-        if (v1) {
-            if (!tc_supported(*a)) return PLKV_ERR_UNSUPPORTED;
-            e = launch_latent_partial_tc(*a, ws, (cudaStream_t)stream);
-        } else {
-            if (!tc2_supported(*a)) return PLKV_ERR_UNSUPPORTED;
-            e = launch_latent_partial_tc2(*a, ws, (cudaStream_t)stream);
-        }
+        if (!tc_supported(*a)) return PLKV_ERR_UNSUPPORTED;
+        e = launch_latent_partial_tc(*a, ws, (cudaStream_t)stream);
     } else {
         e = launch_latent_partial_exact(*a, ws, (cudaStream_t)stream);
     }

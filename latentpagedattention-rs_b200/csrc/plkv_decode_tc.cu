@@ -673,11 +673,6 @@ static bool encode_f16(CUtensorMap* map, const void* base, int rank, const cuuin
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool encode_f16_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
-                    const cuuint64_t* strides, const cuuint32_t* box) {
-    return load_encode() && encode_f16(map, base, rank, dims, strides, box);
-}
-
 bool encode_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank,
                 const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
                 CUtensorMapSwizzle swizzle) {
