@@ -379,7 +379,9 @@ def run_ours(args, s, rank: int, world: int):
     last = {}                                               # attention-level result of a step
     # --grow: every step allocates one new token per sequence on the device;
     # room for all the steps this run takes (warm-up, eager, graph, e2e).
-    grow_steps = args.warmup + 3 * args.steps + 16 if args.grow else 0
+    # warm-up, eager, graph and end-to-end steps (the latter at least 30), and
+    # the parity step
+    grow_steps = args.warmup + 3 * args.steps + max(30, args.steps) + 16 if args.grow else 0
     extra_blocks = s.batch * (grow_steps // s.block_size + 2) if args.grow else 0
     x = wl.device_inputs(s, dev, shards=world if split_k else 1, shard=rank if split_k else 0,
                          with_out_proj=args.with_wo, extra_blocks=extra_blocks)
@@ -765,7 +767,9 @@ def run_ours(args, s, rank: int, world: int):
     e2e = None
     if not args.no_e2e:
         barrier()
-        n_e2e = max(3, args.steps // 2)
+        # the first step's host-to-device copy has nothing to overlap (the
+        # pipeline fills); enough steps that it does not dominate
+        n_e2e = max(30, args.steps)
         e2e_ms, h2d, d2h = e2e_pipelined(stepper, q_buf, rows_buf, n_e2e, dev)
         steps_done += n_e2e + 3
         te = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
