@@ -25,6 +25,9 @@ cudaError_t launch_latent_partial_exact(const plkv_latent_decode_args&, DecodeWo
 cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args&, DecodeWorkspace,
                                      cudaStream_t);
 bool tc_supported(const plkv_latent_decode_args&);
+bool latent_gqa_tc_supported(const plkv_latent_decode_args&);
+cudaError_t launch_latent_partial_gqa_tc(const plkv_latent_decode_args&, DecodeWorkspace,
+                                         cudaStream_t);
 bool fullkv_tc_supported(const plkv_fullkv_decode_args&);
 cudaError_t launch_fullkv_partial_tc(const plkv_fullkv_decode_args&, DecodeWorkspace,
                                      cudaStream_t);
@@ -315,6 +318,10 @@ int plkv_latent_decode_partial(const plkv_latent_decode_args* a, plkv_stream_t s
     if (a->mode == PLKV_MODE_TC_F16) {
         if (!tc_supported(*a)) return PLKV_ERR_UNSUPPORTED;
         e = launch_latent_partial_tc(*a, ws, (cudaStream_t)stream);
+    } else if (latent_gqa_tc_supported(*a)) {
+        // exact mode, GQA-latent shapes without intermediates: tensor cores
+        // with the query and probabilities split into FP16 hi + lo
+        e = launch_latent_partial_gqa_tc(*a, ws, (cudaStream_t)stream);
     } else {
         e = launch_latent_partial_exact(*a, ws, (cudaStream_t)stream);
     }

@@ -47,6 +47,7 @@
 #include <cuda_fp16.h>
 
 #include "plkv_sm100.cuh"
+#include "plkv_tc1.cuh"
 
 namespace plkv {
 namespace tc {
@@ -55,6 +56,7 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, in
                 CUtensorMapSwizzle swizzle);
 }
 namespace fkv {
+using namespace tc1;
 
 constexpr int kTok = 128;        // tokens per tile
 constexpr int kD = 128;          // head_dim
@@ -95,83 +97,6 @@ enum : uint32_t {
 static_assert(kAbort + 4 <= kRedMax, "barriers");
 static_assert(kVote + 16 <= kMiscBytes, "misc region");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
-
-__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                        uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(dst_smem), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
-                 ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// 32 lanes x 16 consecutive 32-bit columns: thread i of the warp gets lane
-// (warp's quarter * 32 + i), columns [col, col + 16).
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float* v) {
-    uint32_t r[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(v[i]);
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
-          "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),
-          "r"(r[13]), "r"(r[14]), "r"(r[15])
-        : "memory");
-}
-
-// A 16-token box (2 x 8 rows, both 64-column halves) of the 4-D pool view at
-// 8-row group index `grp`; completes on `bar` of this CTA.
-__device__ __forceinline__ void tma_chunk(uint32_t dst, const CUtensorMap* map, int grp,
-                                          uint32_t bar, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;"
-        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(0), "r"(grp),
-          "r"(bar), "l"(policy)
-        : "memory");
-}
-
-__device__ __forceinline__ void named_sync_softmax() {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-}
-
-__device__ __forceinline__ float fast_exp2(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 
 // Byte offset of element (row, k) of a 16-row FP16 operand stored K-major in
 // 128-byte-swizzled 64-column blocks (Q^T's and P^T's rows are the heads).

@@ -172,3 +172,48 @@ def test_stale_timeout_bit_does_not_end_a_later_call(ops):
         assert torch.count_nonzero(got) == got.numel()
         assert torch.equal(got, clean)
     assert int(flags.item()) == 0x20                                 # reported bits are kept
+
+
+@pytest.mark.parametrize("L,Hq,bs,target", [(256, 32, 16, None), (256, 32, 16, 40),
+                                            (128, 32, 64, None), (256, 8, 32, 17)])
+def test_gqa_latent_tensor_core_pass_vs_oracle(ops, L, Hq, bs, target):
+    """The exact mode's tensor-core pass (latent = value width 128 / 256, up
+    to 32 heads, no intermediates): lengths around the 128-token tile, several
+    work items per sequence, unused pool slots holding NaN / Inf; equal to the
+    FP64 restatement at 1e-5, and to the CUDA-core pass (taken when scores
+    are requested) in context and log-sum-exp."""
+    KV = 8 if Hq >= 8 else Hq
+    lens = [1, 127, 128, 129, 1000, 3001]
+    c = _gqa_case(70 + L + Hq, lens, L, L, Hq=Hq, KV=KV, bs=bs)
+    used = np.zeros(c["cache"].shape[:2], bool)
+    for b, n in enumerate(c["lens"]):
+        for tok in range(n):
+            used[c["tables"][b, tok // bs], tok % bs] = True
+    pb, pt = np.nonzero(~used)
+    c["cache"][pb[0::2], pt[0::2]] = np.float16(np.nan)
+    c["cache"][pb[1::2], pt[1::2]] = np.float16(np.inf)
+    D = c["D"]
+    cache = t(c["cache"])
+    q_lat = ops.project_query(t(c["q"]), _head_major(c["w_k"], KV, D))
+    plan = (ops.plan_splits(c["lens"], bs, target_items=target) if target
+            else ops.plan_splits(c["lens"], bs))
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kw = dict(scale=1 / math.sqrt(D), value_dim=L, w_v=_head_major(c["w_v"], KV, D),
+              want_lse=True, flags=flags)
+    r = ops.latent_decode(q_lat, cache, t(c["tables"]), t(c["lens"]), plan, **kw)
+    rc = ops.latent_decode(q_lat, cache, t(c["tables"]), t(c["lens"]), plan, want_scores=True,
+                           max_seq_len=int(c["lens"].max()), **kw)
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
+    ctx = r["ctx"].cpu().numpy()
+    assert np.isfinite(ctx).all()
+    assert rel_err(ctx, rc["ctx"].cpu().numpy()) <= EXACT_REL
+    assert rel_err(r["lse"].cpu().numpy(), rc["lse"].cpu().numpy()) <= EXACT_REL
+    bits = c["cache"].view(np.uint16)
+    for b, n in enumerate(c["lens"]):
+        ql = c_ref.project_query(c["q"][b], c["w_k"], KV)
+        _, _, _, ec = c_ref.latent_decode_seq(ql, bits, c["tables"][b], int(n), int(n), bs,
+                                              1 / math.sqrt(D), value_dim=L,
+                                              w_v_canonical=c["w_v"], proj_heads=KV,
+                                              head_dim=D, acc64=True, want_intermediates=False)
+        assert rel_err(ctx[b], ec) <= EXACT_REL, (L, b, rel_err(ctx[b], ec))
