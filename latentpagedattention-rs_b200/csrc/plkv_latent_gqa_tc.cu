@@ -50,6 +50,8 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, in
 }
 namespace lgq {
 using namespace tc1;
+using sm100::tmem_ld32;
+using sm100::tmem_st32;
 
 constexpr int kTok = 128;          // tokens per tile
 constexpr int kHeads = 32;         // query heads, padded
@@ -90,8 +92,10 @@ enum : uint32_t {
     kTmemSlot = 112,
     kAbort = 116,
     kVote = 128,             // [4 warps] int
-    kRedMax = 256,           // [4 warps][32] float
-    kRedSum = 768,           // [4 warps][32] float
+    kMUse = 256,             // [32] float: running max per head (log2 units)
+    kAlpha = 384,            // [32] float: rescale factor of the tile per head
+    kRedMax = 512,           // [4 warps][32] float
+    kRedSum = 1024,          // [4 warps][32] float
 };
 
 // Byte offset of element (row, k) of a 64-row FP16 operand stored K-major in
@@ -101,16 +105,6 @@ __device__ __forceinline__ uint32_t op_offset(int row, int k) {
     return (uint32_t)(k >> 6) * kOpBlock + (uint32_t)(row >> 3) * 1024u +
            (uint32_t)(row & 7) * 128u + ((((uint32_t)(k & 63) >> 3) ^ (uint32_t)(row & 7)) << 4) +
            (uint32_t)(k & 7) * 2u;
-}
-
-// 32 lanes x 64 consecutive columns as two loads of 32.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
-    sm100::tmem_ld32(taddr, v);
-    sm100::tmem_ld32(taddr + 32, v + 32);
-}
-__device__ __forceinline__ void tmem_st64(uint32_t taddr, const float* v) {
-    sm100::tmem_st32(taddr, v);
-    sm100::tmem_st32(taddr + 32, v + 32);
 }
 
 // grid = n_items, block = 192, one CTA per SM.
@@ -327,12 +321,16 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
         float* red_max = reinterpret_cast<float*>(misc + kRedMax);
         float* red_sum = reinterpret_cast<float*>(misc + kRedSum);
         int* vote = reinterpret_cast<int*>(misc + kVote);
-        float m_use[kHeads], l_t[kHeads];
+        // m_use (shared memory): the running max per head, the same for
+        // every thread; l_t: this thread's share of the row sums (its
+        // token's probabilities), reduced over the CTA in the epilogue.
+        float* m_use = reinterpret_cast<float*>(misc + kMUse);
+        float* alpha = reinterpret_cast<float*>(misc + kAlpha);
+        float l_t[kHeads];
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-            m_use[h] = -INFINITY;
-            l_t[h] = 0.f;
-        }
+        for (int h = 0; h < kHeads; ++h) l_t[h] = 0.f;
+        if (tid < kHeads) m_use[tid] = -INFINITY;
+        named_sync_softmax();
         // This thread's token of tile j: inside the item and of a block inside
         // the pool; looked up a tile ahead.
         auto token_ok = [&](int j) -> bool {
@@ -351,26 +349,27 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
             tok_next = token_ok(j + 1);
             if (ok)
                 ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarSFull + 8 * sb, (j >> 1) & 1, wc));
-            float s[kN];
+            float s[kHeads];   // scores, then probabilities
             if (ok) {
+                float lo[kHeads];
                 tc_fence_after();
-                tmem_ld64(tmem + lane_base + C::kColS + 64 * sb, s);
+                tmem_ld32(tmem + lane_base + C::kColS + 64 * sb, s);
+                tmem_ld32(tmem + lane_base + C::kColS + 64 * sb + kHeads, lo);
                 tmem_wait_ld();
+#pragma unroll
+                for (int h = 0; h < kHeads; ++h) s[h] += lo[h];   // Q_hi . L + Q_lo . L
             }
             const bool valid = ok && tok_ok;
             bool above = false;
 #pragma unroll
             for (int h = 0; h < kHeads; ++h) {
-                s[h] = (valid && h < Hq) ? (s[h] + s[kHeads + h]) * scale_log2 : -INFINITY;
+                s[h] = (valid && h < Hq) ? s[h] * scale_log2 : -INFINITY;
                 above |= s[h] > m_use[h] + kTau;
             }
             above = __any_sync(0xffffffffu, above);
             if (lane == 0) vote[warp] = above ? 1 : 0;
             named_sync_softmax();
             const bool resc = (vote[0] | vote[1] | vote[2] | vote[3]) != 0;
-            float alpha[kHeads];
-#pragma unroll
-            for (int h = 0; h < kHeads; ++h) alpha[h] = 1.f;
             if (resc) {
 #pragma unroll
                 for (int h = 0; h < kHeads; ++h) {
@@ -380,28 +379,24 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
                     }
                 }
                 named_sync_softmax();
-#pragma unroll
-                for (int h = 0; h < kHeads; ++h) {
-                    if (h < Hq) {
-                        const float mt =
-                            fmaxf(fmaxf(red_max[h], red_max[kHeads + h]),
-                                  fmaxf(red_max[2 * kHeads + h], red_max[3 * kHeads + h]));
-                        const float m_new = fmaxf(m_use[h], mt);
-                        if (m_new > m_use[h]) {
-                            alpha[h] = (m_use[h] == -INFINITY) ? 0.f : fast_exp2(m_use[h] - m_new);
-                            m_use[h] = m_new;
-                            l_t[h] *= alpha[h];
-                        }
-                    }
+                if (tid < kHeads) {   // warp 0: the new max and factor of head tid
+                    const int h = tid;
+                    const float mt = fmaxf(fmaxf(red_max[h], red_max[kHeads + h]),
+                                           fmaxf(red_max[2 * kHeads + h], red_max[3 * kHeads + h]));
+                    const float m_old = m_use[h], m_new = fmaxf(m_old, mt);
+                    float a = 1.f;
+                    if (m_new > m_old) a = (m_old == -INFINITY) ? 0.f : fast_exp2(m_old - m_new);
+                    m_use[h] = m_new;
+                    alpha[h] = a;
                 }
-                // the votes and maxima are read; the next tile may write them
                 named_sync_softmax();
+#pragma unroll
+                for (int h = 0; h < kHeads; ++h) l_t[h] *= alpha[h];
             }
-            float p[kHeads];
 #pragma unroll
             for (int h = 0; h < kHeads; ++h) {
-                p[h] = (h < Hq && s[h] != -INFINITY) ? fast_exp2(s[h] - m_use[h]) : 0.f;
-                l_t[h] += p[h];
+                s[h] = (h < Hq && s[h] != -INFINITY) ? fast_exp2(s[h] - m_use[h]) : 0.f;
+                l_t[h] += s[h];
             }
             if (ok && resc && j > 0) {
                 // O^T through tile j - 1 must be complete before it is rescaled
@@ -410,20 +405,19 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
                 if (ok) {
                     tc_fence_after();
 #pragma unroll 1
-                    for (int m = 0; m < C::kMB; ++m) {
-                        float o[kN];
-                        tmem_ld64(tmem + lane_base + C::kColO + 64 * m, o);
+                    for (int c = 0; c < 2 * C::kMB; ++c) {   // 32 columns: hi or lo of block c / 2
+                        float o[kHeads];
+                        const uint32_t col = C::kColO + 32 * c;
+                        tmem_ld32(tmem + lane_base + col, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int h = 0; h < kHeads; ++h) {
-                            o[h] *= alpha[h];
-                            o[kHeads + h] *= alpha[h];
-                        }
-                        tmem_st64(tmem + lane_base + C::kColO + 64 * m, o);
+                        for (int h = 0; h < kHeads; ++h) o[h] *= alpha[h];
+                        tmem_st32(tmem + lane_base + col, o);
                     }
                     tmem_wait_st();
                 }
             }
+            const float* p = s;
             // P buffer sb was last read by O of tile j - 2
             if (ok && j >= 2)
                 ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * sb,
@@ -482,21 +476,19 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
         const int64_t row0 = (int64_t)blockIdx.x * Hq;
 #pragma unroll 1
         for (int m = 0; m < C::kMB; ++m) {
-            float o[kN];
+            float o[kHeads], lo[kHeads];
             if (have) {
-                tmem_ld64(tmem + lane_base + C::kColO + 64 * m, o);
+                tmem_ld32(tmem + lane_base + C::kColO + 64 * m, o);
+                tmem_ld32(tmem + lane_base + C::kColO + 64 * m + kHeads, lo);
                 tmem_wait_ld();
             }
 #pragma unroll
             for (int h = 0; h < kHeads; ++h)
                 if (h < Hq)   // thread tid = value dimension 128 m + tid
-                    ws.part_ctx[(row0 + h) * L + 128 * m + tid] = have ? o[h] + o[kHeads + h] : 0.f;
+                    ws.part_ctx[(row0 + h) * L + 128 * m + tid] = have ? o[h] + lo[h] : 0.f;
         }
         if (tid < Hq) {
-            float mh = -INFINITY;
-#pragma unroll
-            for (int h = 0; h < kHeads; ++h)
-                if (h == tid) mh = m_use[h];
+            const float mh = m_use[tid];
             const float l = red_sum[tid] + red_sum[kHeads + tid] + red_sum[2 * kHeads + tid] +
                             red_sum[3 * kHeads + tid];
             ws.part_m[row0 + tid] = (have && mh != -INFINITY) ? mh * kLn2 : -INFINITY;
