@@ -87,6 +87,9 @@ def parse_args():
                     help="time every kernel of the library on one synthetic case each")
     ap.add_argument("--suite-reps", type=int, default=5,
                     help="timed calls per kernel in --kernel-suite (after up to 2 warm-up calls)")
+    ap.add_argument("--suite-only", default="",
+                    help="--kernel-suite: run only the operations whose name contains one of "
+                         "these comma-separated texts (profiling a kernel on its suite case)")
     ap.add_argument("--seqs", type=int, default=0,
                     help="keep only the first N sequences (small profiling cases)")
     return ap.parse_args()
@@ -460,7 +463,7 @@ def run_ours(args, s, rank: int, world: int):
         # every active token, then the same full-KV decode).
         KV, bs = s.kv_heads, s.block_size
         P = x["cache"].shape[0]
-        plan = ops.plan_splits(lens_host, bs, device=dev)
+        plan = ops.plan_fullkv(lens_host, bs, KV, device=dev)
         ctx = torch.empty((nb_local, s.q_heads, D), dtype=torch.float32, device=dev)
         fws = torch.empty(int(ops.lib().plkv_fullkv_decode_workspace_size(
             plan.n_items, nb_local, s.q_heads, D)), dtype=torch.uint8, device=dev)
@@ -1124,6 +1127,8 @@ def run_kernel_suite(args) -> dict:
         """Device time per call: `reps` calls recorded into a CUDA graph and
         replayed (launched from Python, calls of a few microseconds would
         time the host); eager when the call cannot be captured."""
+        if args.suite_only and not any(w in name for w in args.suite_only.split(",")):
+            return
         for _ in range(min(2, reps)):
             fn()
         torch.cuda.synchronize(dev)
@@ -1214,9 +1219,11 @@ def run_kernel_suite(args) -> dict:
                      device=dev)
     ctx = torch.empty((B, Hq, D), **f32)
     kw = dict(scale=1 / math.sqrt(D), value_dim=Lg, w_v=w_v, mode="exact", out=ctx, workspace=ws)
-    timed("latent decode, exact partial pass (64 x 4096 tokens, GQA)", ["latent_partial_exact_kernel"],
+    timed("latent decode, exact-mode partial pass (64 x 4096 tokens, GQA, L = 256)",
+          ["latent_gqa_tc_kernel"],
           lambda: ops.latent_decode(qlat_buf, cache, tables, lens, plan, phase="partial", **kw),
-          B * n_tok * Lg * 2 + B * Hq * Lg * 4, "FP32 CUDA-core bound (64 FLOP/byte)")
+          B * n_tok * Lg * 2 + B * Hq * Lg * 4,
+          "tensor cores, FP16 hi + lo query and probabilities (FP32-accurate)")
     timed("latent decode, exact combine + W_v", ["merge_rows_kernel", "project_rows_kernel"],
           lambda: ops.latent_decode(qlat_buf, cache, tables, lens, plan, phase="combine", **kw),
           plan.n_items * Hq * (Lg + 2) * 4 + w_v.numel() * 4 + ctx.numel() * 4)
@@ -1232,11 +1239,12 @@ def run_kernel_suite(args) -> dict:
                                      v_out=v16),
           n_act * (Lg * 2 + 8 + 2 * KV * D * 2) + (w_k.numel() + w_v.numel()) * 4,
           "FP32 CUDA-core bound (2 x 256 x 2048 FLOP per row)")
-    fws = torch.empty(int(ops.lib().plkv_fullkv_decode_workspace_size(plan.n_items, B, Hq, D)),
+    fplan = ops.plan_fullkv(lens_h, bs, KV, device=dev)
+    fws = torch.empty(int(ops.lib().plkv_fullkv_decode_workspace_size(fplan.n_items, B, Hq, D)),
                       dtype=torch.uint8, device=dev)
     timed("full-KV decode (64 x 4096 tokens, 8 KV heads, FP16)",
           ["fullkv_partial_tc_kernel", "merge_rows_kernel"],
-          lambda: ops.fullkv_decode(qg, k16, v16, tables, lens, plan, scale=1 / math.sqrt(D),
+          lambda: ops.fullkv_decode(qg, k16, v16, tables, lens, fplan, scale=1 / math.sqrt(D),
                                     out=ctx, workspace=fws),
           B * n_tok * KV * D * 2 * 2 + qg.numel() * 4 + ctx.numel() * 4)
     kr, vr = randn(B, KV, D), randn(B, KV, D)

@@ -39,19 +39,23 @@
 // = head, and the two threads sharing a head (token halves) agree through
 // shared memory, so the CTAs never exchange softmax state.
 //
-// MMA issue is split over four threads of the leader CTA.  One thread issues
+// MMA issue is split over six threads of the leader CTA.  One thread issues
 // a tcgen05.mma every ~60 cycles however small the MMA is, and at N = 64 the
 // tensor pipe finishes one in less; measured on B200, 36 pair MMAs take 1.52
 // us from one issuing warp, 0.83 us from two and 0.49 us from four.  So S is
 // cut along K into four 9-step partials, each accumulated by its own issuer
-// in its own TMEM columns and added by the softmax threads; issuers 0 and 1
-// also issue the two 256-column halves of O.  Barriers completed by MMA
-// commits count one arrival per issuer that commits to them.
+// in its own TMEM columns and added by the softmax threads.  Two more threads
+// issue the two 256-column halves of O, so that a tile's S never waits
+// behind the O instructions of the previous tile in an issuer's program
+// order (303 against 310 us per long-context pass on the same B200).
+// Barriers completed by MMA commits count one arrival per issuer that
+// commits to them.
 //
-// Warp roles per CTA: 0 = Q and K loads, 1 = TMEM allocation and (leader CTA)
-// MMA issue, 2 = V loads, 3, 8, 9 = (leader CTA) MMA issue, 4..7 = softmax and
-// epilogue.  Every barrier wait is bounded (1 s): on expiry the kernel records
-// PLKV_FLAG_TIMEOUT, abandons its work, releases tensor memory and exits.
+// Warp roles per CTA: 0 = Q and K loads, 1 = TMEM allocation and (leader
+// CTA) S issue, 2 = V loads, 3, 8, 9 = (leader CTA) S issue, 4..7 = softmax
+// and epilogue, 10, 11 = (leader CTA) O issue.  Every barrier wait is bounded
+// (1 s): on expiry the kernel records PLKV_FLAG_TIMEOUT, abandons its work,
+// releases tensor memory and exits.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -87,7 +91,8 @@ constexpr uint32_t kVTx = kVStage;                            // own CTA
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSBufs = 2;                                     // S accumulators in TMEM
 constexpr uint32_t kTmemO = 0;                                // O at 0..255
-constexpr int kIssuers = 4;                                   // MMA-issuing threads (warps 1, 3, 8, 9)
+constexpr int kIssuers = 4;                                   // S-issuing threads (warps 1, 3, 8, 9)
+constexpr int kThreads = 384;                                 // warps 10, 11 issue O
 constexpr int kKPer = 36 / kIssuers;                          // S k-steps per issuer
 // S partial p of buffer sb at 256 + 32 (kSBufs p + sb)
 __host__ __device__ constexpr uint32_t s_col(int p, int sb) { return 256u + 32u * (kSBufs * p + sb); }
@@ -188,7 +193,7 @@ __device__ __forceinline__ int half_row(const ItemGeom& g, int j, int h,
     return phys * bs + (hs - lb * bs);
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                          const __grid_constant__ CUtensorMap v_map,
                          const __grid_constant__ CUtensorMap q_map,
@@ -324,12 +329,12 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
             }
         }
         __syncwarp();
-    } else if (warp == 1 || warp == 3 || warp == 8 || warp == 9) {
+    } else if (warp == 1 || warp == 3 || warp >= 8) {
         // ---------------------------------------------- MMA issue (leader)
         // Each issuer schedules its MMAs without blocking: its S partial of
         // tile g as soon as K tile g landed and S buffer g % kSBufs is free
-        // (P of its previous tile was written, so the softmax read it), and,
-        // for issuers 0 and 1, its O half of tile g as soon as P(g) is ready.
+        // (P of its previous tile was written, so the softmax read it); an O
+        // issuer its O half of tile g as soon as P(g) is ready.
         // S work thus stays queued on the tensor pipe while the softmax of
         // earlier tiles runs.  S never crosses into the next item before that
         // item's Q is loaded, which waits until every issuer's S of the
@@ -338,8 +343,8 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
         // is not ready may put the thread to sleep while another one, which
         // is, waits to be noticed (about 0.3 us per tile, measured).
         if (leader && lane == 0) {
-            const int part = warp == 1 ? 0 : warp == 3 ? 1 : warp == 8 ? 2 : 3;
-            const bool has_o = part < 2;  // parts 0 and 1 also issue O half `part`
+            const int part = warp == 1 ? 0 : warp == 3 ? 1 : warp == 8 ? 2 : warp == 9 ? 3 : warp - 10;
+            const bool has_o = warp >= 10;  // warps 10 and 11 issue O half `part`, no S
             const uint32_t id_s = idesc_f16(128, 64, false, false);
             const uint32_t id_o = idesc_f16(128, 256, false, true);
             const int n_items_w = i_end - i_begin;
@@ -352,7 +357,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
             uint64_t idle_since = 0, next_check = 0;
             while (has_o ? oi < n_items_w : si < n_items_w) {
                 bool did = false;
-                if (si < n_items_w) {
+                if (!has_o && si < n_items_w) {
                     if (!s_q && mbar_test_wait(mb + kBarQFull, si & 1)) {
                         s_q = true;
                         tc_fence_after();
@@ -396,7 +401,7 @@ latent_partial_tc_kernel(const __grid_constant__ CUtensorMap k_map,
                         go = item_geom(items, i_begin + oi, seq_lens, bs, cap, flags, false);
                     oj = 0;
                     did = true;
-                } else if (og < sg && mbar_test_wait(mb + kBarPFull + 8 * (og & 1), (og >> 1) & 1) &&
+                } else if (mbar_test_wait(mb + kBarPFull + 8 * (og & 1), (og >> 1) & 1) &&
                            (oj > 0 || oi == 0 || mbar_test_wait(mb + kBarOFree, (oi - 1) & 1))) {
                     tc_fence_after();
                     const int st = og & 1;
@@ -723,7 +728,7 @@ cudaError_t launch_latent_partial_tc(const plkv_latent_decode_args& a, DecodeWor
     if (e != cudaSuccess) return e;
     int32_t* flags = a.err_flags;
     const int workers = (a.worker_item_begin && a.n_workers > 0) ? a.n_workers : a.n_items;
-    tc::latent_partial_tc_kernel<<<2 * workers, 320, tc::kSmemBytes, st>>>(
+    tc::latent_partial_tc_kernel<<<2 * workers, tc::kThreads, tc::kSmemBytes, st>>>(
         k_map, v_map, q_map, a.block_size, a.block_tables, a.max_blocks, a.num_physical,
         a.seq_lens,
         a.items, (a.worker_item_begin && a.n_workers > 0) ? a.worker_item_begin : nullptr, ws,

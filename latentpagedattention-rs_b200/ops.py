@@ -331,6 +331,27 @@ def plan_workers(seq_lens_host, block_size: int, *, n_workers: int | None = None
                       n_workers)
 
 
+FULLKV_MIN_ITEM_TOKENS = 2048
+
+
+def plan_fullkv(seq_lens_host, block_size: int, kv_heads: int, *,
+                device: torch.device | str = "cuda") -> DecodePlan:
+    """Split-K plan for the full-KV decode, whose grid is items x KV heads.
+
+    Items hold at least 2048 tokens (16 tiles of the tensor-core pass, which
+    spends about two tiles' time filling its pipeline), unless the grid would
+    then leave SMs idle.  On a B200, 16 x 4096 tokens (8 KV heads) take 74 us
+    in 32 items against 171 us in the 304 of the default split, and
+    64 x 4096 tokens take 241 us against 323 us."""
+    lens = np.asarray(seq_lens_host, dtype=np.int64)
+    device = torch.device(device)
+    sms = default_target_items(device if device.type == "cuda" else None) // 2
+    total = int(lens.sum())
+    min_tokens = min(FULLKV_MIN_ITEM_TOKENS, max(1, total * max(1, kv_heads) // sms))
+    return plan_splits(lens.astype(np.int32), block_size,
+                       min_blocks=max(1, min_tokens // block_size), device=device)
+
+
 # ------------------------------------------------------------------- decode
 
 def project_query(q: torch.Tensor, w_k_head_major: torch.Tensor, *,

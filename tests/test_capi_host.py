@@ -205,3 +205,25 @@ def test_worker_plan_balances_and_covers(lens, bs, workers):
         eq.append((b - a) + c * n_it)
     assert max(cost) <= max(eq)
     assert max(cost) <= -(-(total + c * len(lens)) // workers) + 2 * c
+
+
+@pytest.mark.parametrize("lens,bs,kv,min_tokens", [
+    ([4096] * 16, 16, 8, 2048), ([4096] * 64, 16, 8, 2048), ([256], 16, 8, 16),
+    ([100, 20000, 7], 32, 1, 20107 // 148)])
+def test_fullkv_plan_item_sizes(lens, bs, kv, min_tokens):
+    """The full-KV planner keeps every item at least `min_tokens` long
+    (except a sequence's whole remainder) and still covers every block once."""
+    import importlib
+
+    ops = importlib.import_module(PACKAGE + ".ops")
+    plan = ops.plan_fullkv(lens, bs, kv, device="cpu")
+    items, begin = plan.items_host, plan.seq_item_begin_host
+    for b, n in enumerate(lens):
+        its = items[begin[b]:begin[b + 1]]
+        nb = (n + bs - 1) // bs
+        covered = np.concatenate([np.arange(i[1], i[2]) for i in its])
+        np.testing.assert_array_equal(covered, np.arange(nb))
+        if len(its) > 1:
+            assert (its[:, 2] - its[:, 1]).min() * bs >= min_tokens // 2
+    if lens == [4096] * 16:
+        assert plan.n_items == 32

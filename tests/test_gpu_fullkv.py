@@ -112,3 +112,22 @@ def test_fullkv_large_scores_rescale():
     c["q"] *= 4
     r = _run(c)
     assert rel_err(r["ctx"].cpu().numpy(), _oracle(c)) <= EXACT_REL
+
+
+def test_fullkv_long_items_from_the_fullkv_planner():
+    """Items of the full-KV planner (at least 2048 tokens each: 16 tiles and
+    more per CTA) against the FP64 oracle."""
+    c = _case(23, [20000, 36001, 300, 16384], 32, 8, 16)
+    ops = _ops()
+    t = lambda a: torch.as_tensor(np.ascontiguousarray(a), device=DEV)
+    plan = ops.plan_fullkv(c["lens"], c["bs"], 8)
+    sizes = plan.items_host[:, 2] - plan.items_host[:, 1]
+    assert plan.n_items <= 40 and np.sort(sizes)[1] * 16 >= 1024
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    r = ops.fullkv_decode(t(c["q"]), t(c["kc"]), t(c["vc"]), t(c["tables"]), t(c["lens"]), plan,
+                          scale=c["scale"], flags=flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
+    got = r["ctx"].cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_err(got, _oracle(c)) <= EXACT_REL
