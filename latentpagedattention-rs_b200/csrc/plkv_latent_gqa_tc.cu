@@ -36,7 +36,8 @@
 // the epilogue; O^T rescaled in tensor memory when the max moves.
 //
 // Warps: 0-3 softmax and epilogue, 4 tensor-memory allocation and (lane 0)
-// MMA issue, 5 loads.  Every wait is bounded (1 s): on expiry the kernel
+// S^T issue, 5 loads, 6 and 7 (lane 0) O^T issue, one 128-dimension block
+// each.  Every wait is bounded (1 s): on expiry the kernel
 // records PLKV_FLAG_TIMEOUT, abandons its work and frees tensor memory.
 #include <cuda_fp16.h>
 
@@ -56,7 +57,7 @@ using sm100::tmem_st32;
 constexpr int kTok = 128;          // tokens per tile
 constexpr int kHeads = 32;         // query heads, padded
 constexpr int kN = 2 * kHeads;     // hi and lo parts stacked
-constexpr int kThreads = 192;
+constexpr int kThreads = 256;
 constexpr float kTau = 8.f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr uint32_t kOpBlock = kN * 128;   // 64 rows x 64 FP16 columns: 8 KiB
@@ -145,12 +146,12 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
     if (tid == 0) {
         for (int s = 0; s < C::kStages; ++s) {
             mbar_init(mb + kBarKVFull + 8 * s, 1);
-            mbar_init(mb + kBarKVEmpty + 8 * s, 1);
+            mbar_init(mb + kBarKVEmpty + 8 * s, C::kMB);   // one commit per O issuer
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(mb + kBarSFull + 8 * i, 1);
             mbar_init(mb + kBarPFull + 8 * i, 1);
-            mbar_init(mb + kBarODone + 8 * i, 1);
+            mbar_init(mb + kBarODone + 8 * i, C::kMB);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -228,9 +229,13 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
             }
             __syncwarp();
         }
-    } else if (warp == 4) {
+    } else if (warp == 4 || warp >= 6) {
         // --------------------------------------------------------- MMA issue
-        if (lane == 0 && n_tiles > 0) {
+        // Warp 4 issues S^T, warp 6 + m block m of O^T: one thread issues a
+        // tcgen05.mma every ~60 cycles, so S of a tile never waits behind
+        // the O instructions of the tile before it in one program order.
+        const int role = warp == 4 ? -1 : warp - 6;   // -1: S^T, else O^T block
+        if (lane == 0 && n_tiles > 0 && role < C::kMB) {
             const uint32_t id_s = idesc_f16(128, kN, false, false);
             const uint32_t id_o = idesc_f16(128, kN, true, false);
             // S^T of tile j (its rows landed; S buffer j & 1 read by the
@@ -249,7 +254,7 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
                 }
                 mma_commit(mb + kBarSFull + 8 * sb);
             };
-            // O^T of tile j (its P written): both parts of P at once
+            // O^T block `role` of tile j (its P written): both parts of P at once
             auto issue_o = [&](int j) {
                 const int st = j % C::kStages, pb = j & 1;
                 tc_fence_after();
@@ -259,34 +264,34 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
                 for (int kt = 0; kt < kTok / 16; ++kt) {
                     const uint64_t bdesc = sdesc_sw128(
                         pbase + (uint32_t)(kt >> 2) * kOpBlock + (uint32_t)(kt & 3) * 32u, 16, 1024);
-#pragma unroll
-                    for (int m = 0; m < C::kMB; ++m)
-                        // Lv^T block m: MN-major, its two 64-dimension column
-                        // blocks 1 KiB apart, 8-token groups one group apart
-                        mma_f16(tmem + C::kColO + 64 * m,
-                                sdesc_sw128(tile + (uint32_t)(2 * m) * 1024u +
-                                                (uint32_t)kt * 2u * C::kGroupBytes,
-                                            1024, C::kGroupBytes),
-                                bdesc, id_o, (j > 0 || kt > 0) ? 1u : 0u);
+                    // Lv^T block `role`: MN-major, its two 64-dimension
+                    // column blocks 1 KiB apart, 8-token groups one group apart
+                    mma_f16(tmem + C::kColO + 64 * role,
+                            sdesc_sw128(tile + (uint32_t)(2 * role) * 1024u +
+                                            (uint32_t)kt * 2u * C::kGroupBytes,
+                                        1024, C::kGroupBytes),
+                            bdesc, id_o, (j > 0 || kt > 0) ? 1u : 0u);
                 }
                 mma_commit(mb + kBarODone + 8 * pb);
                 mma_commit(mb + kBarKVEmpty + 8 * st);
             };
             // Non-blocking: S as soon as its tile landed and its buffer is
-            // free, O as soon as its P is written; bounded as in mbar_wait.
+            // free, O as soon as its P is written (which follows S of the
+            // tile); bounded as in mbar_wait.
             int sj = 0, oj = 0;
             uint64_t idle_since = 0, next_check = 0;
-            while (oj < n_tiles) {
+            while (role < 0 ? sj < n_tiles : oj < n_tiles) {
                 bool did = false;
-                if (sj < n_tiles &&
-                    mbar_test_wait(mb + kBarKVFull + 8 * (sj % C::kStages),
-                                   (sj / C::kStages) & 1) &&
-                    (sj < 2 || mbar_test_wait(mb + kBarPFull + 8 * (sj & 1), ((sj - 2) >> 1) & 1))) {
-                    issue_s(sj);
-                    ++sj;
-                    did = true;
-                }
-                if (oj < sj && mbar_test_wait(mb + kBarPFull + 8 * (oj & 1), (oj >> 1) & 1)) {
+                if (role < 0) {
+                    if (mbar_test_wait(mb + kBarKVFull + 8 * (sj % C::kStages),
+                                       (sj / C::kStages) & 1) &&
+                        (sj < 2 ||
+                         mbar_test_wait(mb + kBarPFull + 8 * (sj & 1), ((sj - 2) >> 1) & 1))) {
+                        issue_s(sj);
+                        ++sj;
+                        did = true;
+                    }
+                } else if (mbar_test_wait(mb + kBarPFull + 8 * (oj & 1), (oj >> 1) & 1)) {
                     issue_o(oj);
                     ++oj;
                     did = true;
