@@ -35,9 +35,9 @@
 // passes the running max by more than 8), row sums kept per thread until
 // the epilogue; O^T rescaled in tensor memory when the max moves.
 //
-// Warps: 0-3 softmax and epilogue, 4 tensor-memory allocation and (lane 0)
-// S^T issue, 5 loads, 6 and 7 (lane 0) O^T issue, one 128-dimension block
-// each.  Every wait is bounded (1 s): on expiry the kernel
+// Warps: 0-7 softmax and epilogue (two per TMEM lane quarter, 16 heads
+// each), 8 tensor-memory allocation and (lane 0) S^T issue, 9 loads, 10 and
+// 11 (lane 0) O^T issue, one 128-dimension block each.  Every wait is bounded (1 s): on expiry the kernel
 // records PLKV_FLAG_TIMEOUT, abandons its work and frees tensor memory.
 #include <cuda_fp16.h>
 
@@ -51,13 +51,14 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, in
 }
 namespace lgq {
 using namespace tc1;
-using sm100::tmem_ld32;
-using sm100::tmem_st32;
 
 constexpr int kTok = 128;          // tokens per tile
 constexpr int kHeads = 32;         // query heads, padded
 constexpr int kN = 2 * kHeads;     // hi and lo parts stacked
-constexpr int kThreads = 256;
+constexpr int kSmWarps = 8;                  // softmax and epilogue warps
+constexpr int kSmThreads = 32 * kSmWarps;
+constexpr int kThreads = kSmThreads + 128;   // + allocation / S issue, loads, two O issuers
+constexpr int kHalf = 16;                    // heads per softmax thread
 constexpr float kTau = 8.f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr uint32_t kOpBlock = kN * 128;   // 64 rows x 64 FP16 columns: 8 KiB
@@ -92,12 +93,16 @@ enum : uint32_t {
     kBarODone = 96,          // [2] MMA commit: O^T through the tile done
     kTmemSlot = 112,
     kAbort = 116,
-    kVote = 128,             // [4 warps] int
+    kVote = 128,             // [8 softmax warps] int
     kMUse = 256,             // [32] float: running max per head (log2 units)
     kAlpha = 384,            // [32] float: rescale factor of the tile per head
-    kRedMax = 512,           // [4 warps][32] float
-    kRedSum = 1024,          // [4 warps][32] float
+    kRedMax = 512,           // [4 lane quarters][32] float
+    kRedSum = 1024,          // [4 lane quarters][32] float
 };
+
+__device__ __forceinline__ void named_sync_sm() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kSmThreads) : "memory");
+}
 
 // Byte offset of element (row, k) of a 64-row FP16 operand stored K-major in
 // 128-byte-swizzled 64-column blocks (rows: the 32 heads' high parts, then
@@ -182,7 +187,7 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
     for (int i = tid; i < (int)(2 * C::kPBytes / 16); i += kThreads)
         reinterpret_cast<uint4*>(smem + C::kPOff)[i] = make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
-    if (warp == 4) {
+    if (warp == kSmWarps) {
         tmem_alloc(mb + kTmemSlot, C::kTmemCols);
         tmem_relinquish();
     }
@@ -191,7 +196,7 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
     tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(misc + kTmemSlot);
 
-    if (warp == 5) {
+    if (warp == kSmWarps + 1) {
         // -------------------------------------------------------------- loads
         // Lane c < 8 resolves box c of a tile (its 8-row group index, or an
         // out-of-bounds index past the item or for a table entry outside the
@@ -229,12 +234,12 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
             }
             __syncwarp();
         }
-    } else if (warp == 4 || warp >= 6) {
+    } else if (warp == kSmWarps || warp >= kSmWarps + 2) {
         // --------------------------------------------------------- MMA issue
-        // Warp 4 issues S^T, warp 6 + m block m of O^T: one thread issues a
+        // Warp 8 issues S^T, warp 10 + m block m of O^T: one thread issues a
         // tcgen05.mma every ~60 cycles, so S of a tile never waits behind
         // the O instructions of the tile before it in one program order.
-        const int role = warp == 4 ? -1 : warp - 6;   // -1: S^T, else O^T block
+        const int role = warp == kSmWarps ? -1 : warp - (kSmWarps + 2);   // -1: S^T, else O^T block
         if (lane == 0 && n_tiles > 0 && role < C::kMB) {
             const uint32_t id_s = idesc_f16(128, kN, false, false);
             const uint32_t id_o = idesc_f16(128, kN, true, false);
@@ -322,26 +327,32 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
         __syncwarp();
     } else {
         // ------------------------------------------------ softmax and epilogue
-        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        // Eight warps: warp w reads TMEM lanes 32 (w & 3) .. + 31 (tokens of
+        // the tile; value dimensions in the epilogue) and handles heads
+        // [16 (w >> 2), + 16), so two warps share each SM sub-partition and
+        // each issues half of a tile's softmax instructions.
+        const int q4 = warp & 3, h0 = kHalf * (warp >> 2);
+        const int t = tid & (kTok - 1);   // token row of the tile
+        const uint32_t lane_base = static_cast<uint32_t>(q4 * 32) << 16;
         float* red_max = reinterpret_cast<float*>(misc + kRedMax);
         float* red_sum = reinterpret_cast<float*>(misc + kRedSum);
         int* vote = reinterpret_cast<int*>(misc + kVote);
         // m_use (shared memory): the running max per head, the same for
-        // every thread; l_t: this thread's share of the row sums (its
-        // token's probabilities), reduced over the CTA in the epilogue.
+        // every thread; l_t: this thread's share of the row sums of its
+        // heads (its token's probabilities), reduced in the epilogue.
         float* m_use = reinterpret_cast<float*>(misc + kMUse);
         float* alpha = reinterpret_cast<float*>(misc + kAlpha);
-        float l_t[kHeads];
+        float l_t[kHalf];
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) l_t[h] = 0.f;
+        for (int h = 0; h < kHalf; ++h) l_t[h] = 0.f;
         if (tid < kHeads) m_use[tid] = -INFINITY;
-        named_sync_softmax();
+        named_sync_sm();
         // This thread's token of tile j: inside the item and of a block inside
         // the pool; looked up a tile ahead.
         auto token_ok = [&](int j) -> bool {
-            const int t = t_begin + j * kTok + tid;
-            if (j >= n_tiles || t >= t_end) return false;
-            const int32_t phys = tables[(int64_t)b * max_blocks + t / bs];
+            const int tt = t_begin + j * kTok + t;
+            if (j >= n_tiles || tt >= t_end) return false;
+            const int32_t phys = tables[(int64_t)b * max_blocks + tt / bs];
             return phys >= 0 && phys < num_physical;
         };
         bool tok_next = token_ok(0);
@@ -354,36 +365,39 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
             tok_next = token_ok(j + 1);
             if (ok)
                 ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarSFull + 8 * sb, (j >> 1) & 1, wc));
-            float s[kHeads];   // scores, then probabilities
+            float s[kHalf];   // scores, then probabilities
             if (ok) {
-                float lo[kHeads];
+                float lo[kHalf];
                 tc_fence_after();
-                tmem_ld32(tmem + lane_base + C::kColS + 64 * sb, s);
-                tmem_ld32(tmem + lane_base + C::kColS + 64 * sb + kHeads, lo);
+                tmem_ld16(tmem + lane_base + C::kColS + 64 * sb + h0, s);
+                tmem_ld16(tmem + lane_base + C::kColS + 64 * sb + kHeads + h0, lo);
                 tmem_wait_ld();
 #pragma unroll
-                for (int h = 0; h < kHeads; ++h) s[h] += lo[h];   // Q_hi . L + Q_lo . L
+                for (int h = 0; h < kHalf; ++h) s[h] += lo[h];   // Q_hi . L + Q_lo . L
             }
             const bool valid = ok && tok_ok;
             bool above = false;
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h) {
-                s[h] = (valid && h < Hq) ? s[h] * scale_log2 : -INFINITY;
-                above |= s[h] > m_use[h] + kTau;
+            for (int h = 0; h < kHalf; ++h) {
+                s[h] = (valid && h0 + h < Hq) ? s[h] * scale_log2 : -INFINITY;
+                above |= s[h] > m_use[h0 + h] + kTau;
             }
             above = __any_sync(0xffffffffu, above);
             if (lane == 0) vote[warp] = above ? 1 : 0;
-            named_sync_softmax();
-            const bool resc = (vote[0] | vote[1] | vote[2] | vote[3]) != 0;
+            named_sync_sm();
+            int any = 0;
+#pragma unroll
+            for (int w = 0; w < kSmWarps; ++w) any |= vote[w];
+            const bool resc = any != 0;
             if (resc) {
 #pragma unroll
-                for (int h = 0; h < kHeads; ++h) {
-                    if (h < Hq) {
+                for (int h = 0; h < kHalf; ++h) {
+                    if (h0 + h < Hq) {
                         const float mx = warp_max(s[h]);
-                        if (lane == 0) red_max[warp * kHeads + h] = mx;
+                        if (lane == 0) red_max[q4 * kHeads + h0 + h] = mx;
                     }
                 }
-                named_sync_softmax();
+                named_sync_sm();
                 if (tid < kHeads) {   // warp 0: the new max and factor of head tid
                     const int h = tid;
                     const float mt = fmaxf(fmaxf(red_max[h], red_max[kHeads + h]),
@@ -394,13 +408,13 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
                     m_use[h] = m_new;
                     alpha[h] = a;
                 }
-                named_sync_softmax();
+                named_sync_sm();
 #pragma unroll
-                for (int h = 0; h < kHeads; ++h) l_t[h] *= alpha[h];
+                for (int h = 0; h < kHalf; ++h) l_t[h] *= alpha[h0 + h];
             }
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h) {
-                s[h] = (h < Hq && s[h] != -INFINITY) ? fast_exp2(s[h] - m_use[h]) : 0.f;
+            for (int h = 0; h < kHalf; ++h) {
+                s[h] = (h0 + h < Hq && s[h] != -INFINITY) ? fast_exp2(s[h] - m_use[h0 + h]) : 0.f;
                 l_t[h] += s[h];
             }
             if (ok && resc && j > 0) {
@@ -410,14 +424,14 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
                 if (ok) {
                     tc_fence_after();
 #pragma unroll 1
-                    for (int c = 0; c < 2 * C::kMB; ++c) {   // 32 columns: hi or lo of block c / 2
-                        float o[kHeads];
-                        const uint32_t col = C::kColO + 32 * c;
-                        tmem_ld32(tmem + lane_base + col, o);
+                    for (int c = 0; c < 2 * C::kMB; ++c) {   // hi or lo part of block c / 2
+                        float o[kHalf];
+                        const uint32_t col = C::kColO + 64 * (c >> 1) + kHeads * (c & 1) + h0;
+                        tmem_ld16(tmem + lane_base + col, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int h = 0; h < kHeads; ++h) o[h] *= alpha[h];
-                        tmem_st32(tmem + lane_base + col, o);
+                        for (int h = 0; h < kHalf; ++h) o[h] *= alpha[h0 + h];
+                        tmem_st16(tmem + lane_base + col, o);
                     }
                     tmem_wait_st();
                 }
@@ -430,12 +444,12 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
             if (ok) {
                 uint8_t* pb = smem + C::kPOff + (uint32_t)sb * C::kPBytes;
 #pragma unroll
-                for (int h = 0; h < kHeads; ++h) {
-                    if (h < Hq) {
+                for (int h = 0; h < kHalf; ++h) {
+                    if (h0 + h < Hq) {
                         const __half hi = __float2half_rn(p[h]);
                         const __half lo = __float2half_rn(p[h] - __half2float(hi));
-                        *reinterpret_cast<__half*>(pb + op_offset(h, tid)) = hi;
-                        *reinterpret_cast<__half*>(pb + op_offset(kHeads + h, tid)) = lo;
+                        *reinterpret_cast<__half*>(pb + op_offset(h0 + h, t)) = hi;
+                        *reinterpret_cast<__half*>(pb + op_offset(kHeads + h0 + h, t)) = lo;
                     }
                 }
             }
@@ -450,7 +464,7 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
                 if (ok) {
                     uint8_t* tile = smem + (uint32_t)st * C::kTileBytes;
                     const int rows = 16 - (nt & 15);
-                    for (int i = tid; i < rows * C::kCB * 8; i += 128) {
+                    for (int i = tid; i < rows * C::kCB * 8; i += kSmThreads) {
                         const int r = nt + i / (C::kCB * 8), rem = i % (C::kCB * 8);
                         const int cb = rem >> 3, c16 = rem & 7;
                         *reinterpret_cast<uint4*>(tile + (uint32_t)(r >> 3) * C::kGroupBytes +
@@ -461,7 +475,7 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
             }
             fence_proxy_async_smem();
             tc_fence_before();
-            named_sync_softmax();
+            named_sync_sm();
             if (ok && tid == 0) mbar_arrive_local(mb + kBarPFull + 8 * sb);
         }
         // Epilogue: this item's (m, l, context) for the Hq heads.
@@ -469,28 +483,28 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
             ok = __all_sync(0xffffffffu, mbar_wait(mb + kBarODone + 8 * ((n_tiles - 1) & 1),
                                                    ((n_tiles - 1) >> 1) & 1, wc));
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-            if (h < Hq) {
+        for (int h = 0; h < kHalf; ++h) {
+            if (h0 + h < Hq) {
                 const float lw = warp_sum(l_t[h]);
-                if (lane == 0) red_sum[warp * kHeads + h] = lw;
+                if (lane == 0) red_sum[q4 * kHeads + h0 + h] = lw;
             }
         }
-        named_sync_softmax();
+        named_sync_sm();
         const bool have = ok && n_tiles > 0;
         if (have) tc_fence_after();
         const int64_t row0 = (int64_t)blockIdx.x * Hq;
 #pragma unroll 1
         for (int m = 0; m < C::kMB; ++m) {
-            float o[kHeads], lo[kHeads];
+            float o[kHalf], lo[kHalf];
             if (have) {
-                tmem_ld32(tmem + lane_base + C::kColO + 64 * m, o);
-                tmem_ld32(tmem + lane_base + C::kColO + 64 * m + kHeads, lo);
+                tmem_ld16(tmem + lane_base + C::kColO + 64 * m + h0, o);
+                tmem_ld16(tmem + lane_base + C::kColO + 64 * m + kHeads + h0, lo);
                 tmem_wait_ld();
             }
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h)
-                if (h < Hq)   // thread tid = value dimension 128 m + tid
-                    ws.part_ctx[(row0 + h) * L + 128 * m + tid] = have ? o[h] + lo[h] : 0.f;
+            for (int h = 0; h < kHalf; ++h)
+                if (h0 + h < Hq)   // thread = value dimension 128 m + t
+                    ws.part_ctx[(row0 + h0 + h) * L + 128 * m + t] = have ? o[h] + lo[h] : 0.f;
         }
         if (tid < Hq) {
             const float mh = m_use[tid];
@@ -505,7 +519,7 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 4) tmem_dealloc(tmem, C::kTmemCols);
+    if (warp == kSmWarps) tmem_dealloc(tmem, C::kTmemCols);
 }
 
 template <int L>
