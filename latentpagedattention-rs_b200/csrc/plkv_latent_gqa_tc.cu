@@ -55,10 +55,19 @@ using namespace tc1;
 constexpr int kTok = 128;          // tokens per tile
 constexpr int kHeads = 32;         // query heads, padded
 constexpr int kN = 2 * kHeads;     // hi and lo parts stacked
-constexpr int kSmWarps = 8;                  // softmax and epilogue warps
+constexpr int kSmWarps = 16;                 // softmax and epilogue warps
 constexpr int kSmThreads = 32 * kSmWarps;
 constexpr int kThreads = kSmThreads + 128;   // + allocation / S issue, loads, two O issuers
-constexpr int kHalf = 16;                    // heads per softmax thread
+constexpr int kHalf = kHeads / (kSmWarps / 4);   // heads per softmax thread
+static_assert(kHalf == 8 || kHalf == 16, "TMEM access width");
+
+// kHalf consecutive TMEM columns of the warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld_heads(uint32_t taddr, float* v) {
+    if constexpr (kHalf == 16) tmem_ld16(taddr, v); else tmem_ld8(taddr, v);
+}
+__device__ __forceinline__ void tmem_st_heads(uint32_t taddr, const float* v) {
+    if constexpr (kHalf == 16) tmem_st16(taddr, v); else tmem_st8(taddr, v);
+}
 constexpr float kTau = 8.f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr uint32_t kOpBlock = kN * 128;   // 64 rows x 64 FP16 columns: 8 KiB
@@ -369,8 +378,8 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
             if (ok) {
                 float lo[kHalf];
                 tc_fence_after();
-                tmem_ld16(tmem + lane_base + C::kColS + 64 * sb + h0, s);
-                tmem_ld16(tmem + lane_base + C::kColS + 64 * sb + kHeads + h0, lo);
+                tmem_ld_heads(tmem + lane_base + C::kColS + 64 * sb + h0, s);
+                tmem_ld_heads(tmem + lane_base + C::kColS + 64 * sb + kHeads + h0, lo);
                 tmem_wait_ld();
 #pragma unroll
                 for (int h = 0; h < kHalf; ++h) s[h] += lo[h];   // Q_hi . L + Q_lo . L
@@ -427,11 +436,11 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
                     for (int c = 0; c < 2 * C::kMB; ++c) {   // hi or lo part of block c / 2
                         float o[kHalf];
                         const uint32_t col = C::kColO + 64 * (c >> 1) + kHeads * (c & 1) + h0;
-                        tmem_ld16(tmem + lane_base + col, o);
+                        tmem_ld_heads(tmem + lane_base + col, o);
                         tmem_wait_ld();
 #pragma unroll
                         for (int h = 0; h < kHalf; ++h) o[h] *= alpha[h0 + h];
-                        tmem_st16(tmem + lane_base + col, o);
+                        tmem_st_heads(tmem + lane_base + col, o);
                     }
                     tmem_wait_st();
                 }
@@ -497,8 +506,8 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
         for (int m = 0; m < C::kMB; ++m) {
             float o[kHalf], lo[kHalf];
             if (have) {
-                tmem_ld16(tmem + lane_base + C::kColO + 64 * m + h0, o);
-                tmem_ld16(tmem + lane_base + C::kColO + 64 * m + kHeads + h0, lo);
+                tmem_ld_heads(tmem + lane_base + C::kColO + 64 * m + h0, o);
+                tmem_ld_heads(tmem + lane_base + C::kColO + 64 * m + kHeads + h0, lo);
                 tmem_wait_ld();
             }
 #pragma unroll
