@@ -170,42 +170,53 @@ latent_gqa_tc_kernel(const __grid_constant__ CUtensorMap map, int64_t n_groups,
         *abort_flag = 0;
         fence_mbar_init();
     }
-    // Q^T: head h's high part in row h, its low part in row 32 + h (rows of
-    // heads >= Hq zero); both P buffers zero (rows of heads >= Hq stay so).
-    {
-        constexpr int kBatch = 16;
-        for (int i0 = tid; i0 < kHeads * L; i0 += kBatch * kThreads) {
-            float qv[kBatch];
+    // The loader starts on the first tiles as soon as the barriers exist;
+    // the other warps stage Q^T, clear P and allocate tensor memory in the
+    // meantime and meet at a named barrier without it.
+    __syncthreads();
+    constexpr int kLoadWarp = kSmWarps + 1;
+    uint32_t tmem = 0;
+    if (warp != kLoadWarp) {
+        if (tid < kSmThreads) {
+            // Q^T: head h's high part in row h, its low part in row 32 + h
+            // (rows of heads >= Hq zero); both P buffers zero (rows of heads
+            // >= Hq stay so).
+            constexpr int kBatch = 16;
+            for (int i0 = tid; i0 < kHeads * L; i0 += kBatch * kSmThreads) {
+                float qv[kBatch];
 #pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                const int i = i0 + u * kThreads, h = i / L, d = i - h * L;
-                qv[u] = (i < kHeads * L && h < Hq) ? q_lat[((int64_t)b * Hq + h) * L + d] : 0.f;
-            }
+                for (int u = 0; u < kBatch; ++u) {
+                    const int i = i0 + u * kSmThreads, h = i / L, d = i - h * L;
+                    qv[u] = (i < kHeads * L && h < Hq) ? q_lat[((int64_t)b * Hq + h) * L + d]
+                                                       : 0.f;
+                }
 #pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                const int i = i0 + u * kThreads, h = i / L, d = i - h * L;
-                if (i < kHeads * L) {
-                    const __half hi = __float2half_rn(qv[u]);
-                    const __half lo = __float2half_rn(qv[u] - __half2float(hi));
-                    *reinterpret_cast<__half*>(smem + C::kQOff + op_offset(h, d)) = hi;
-                    *reinterpret_cast<__half*>(smem + C::kQOff + op_offset(kHeads + h, d)) = lo;
+                for (int u = 0; u < kBatch; ++u) {
+                    const int i = i0 + u * kSmThreads, h = i / L, d = i - h * L;
+                    if (i < kHeads * L) {
+                        const __half hi = __float2half_rn(qv[u]);
+                        const __half lo = __float2half_rn(qv[u] - __half2float(hi));
+                        *reinterpret_cast<__half*>(smem + C::kQOff + op_offset(h, d)) = hi;
+                        *reinterpret_cast<__half*>(smem + C::kQOff + op_offset(kHeads + h, d)) =
+                            lo;
+                    }
                 }
             }
+            for (int i = tid; i < (int)(2 * C::kPBytes / 16); i += kSmThreads)
+                reinterpret_cast<uint4*>(smem + C::kPOff)[i] = make_uint4(0, 0, 0, 0);
+            fence_proxy_async_smem();
         }
+        if (warp == kSmWarps) {
+            tmem_alloc(mb + kTmemSlot, C::kTmemCols);
+            tmem_relinquish();
+        }
+        tc_fence_before();
+        asm volatile("bar.sync 2, %0;" ::"n"(kThreads - 32) : "memory");
+        tc_fence_after();
+        tmem = *reinterpret_cast<volatile uint32_t*>(misc + kTmemSlot);
     }
-    for (int i = tid; i < (int)(2 * C::kPBytes / 16); i += kThreads)
-        reinterpret_cast<uint4*>(smem + C::kPOff)[i] = make_uint4(0, 0, 0, 0);
-    fence_proxy_async_smem();
-    if (warp == kSmWarps) {
-        tmem_alloc(mb + kTmemSlot, C::kTmemCols);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(misc + kTmemSlot);
 
-    if (warp == kSmWarps + 1) {
+    if (warp == kLoadWarp) {
         // -------------------------------------------------------------- loads
         // Lane c < 8 resolves box c of a tile (its 8-row group index, or an
         // out-of-bounds index past the item or for a table entry outside the
