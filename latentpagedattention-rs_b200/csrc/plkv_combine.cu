@@ -190,6 +190,11 @@ cudaError_t launch_project_rows(const float* rows, void* const* rows_table, int 
                                 size_t rows_offset, int B, int Hr, int width, const float* w,
                                 int proj_heads, int D, float* out, cudaStream_t st) {
     const int group = Hr / proj_heads;
+    // 32 or more rows per weight: a tiled GEMM reads each weight once per
+    // 64-row tile, where the row-group kernel below re-reads it every 8 rows
+    // (GQA write_attend, 8192 rows of width 256: 100 us per call).
+    if (!rows_table && (int64_t)B * group >= 32 && rows_gemm_supported(rows, w, out, width, D))
+        return launch_rows_gemm(rows, w, false, out, B, Hr, proj_heads, width, D, st);
     const size_t smem = (size_t)width * 8 * 4 + 8 * 8 * 32 * 4;
     cudaError_t e = cudaFuncSetAttribute(project_rows_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

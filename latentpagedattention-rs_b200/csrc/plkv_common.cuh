@@ -184,4 +184,11 @@ cudaError_t launch_project_rows(const float* rows, void* const* rows_table, int 
                                 size_t rows_offset, int B, int Hr, int width, const float* w,
                                 int proj_heads, int D, float* out, cudaStream_t st);
 
+// c[b, g G + j, :] = W[g] a[b, g G + j, :] for the G = Hq / heads rows of
+// each head g, as a batched FP32 GEMM (plkv_rows_gemm.cu); W[g] is [K][N]
+// row-major, or [N][K] when w_transposed.  Needs rows_gemm_supported.
+bool rows_gemm_supported(const float* a, const float* w, const float* c, int K, int N);
+cudaError_t launch_rows_gemm(const float* a, const float* w, bool w_transposed, float* c, int B,
+                             int Hq, int heads, int K, int N, cudaStream_t st);
+
 }  // namespace plkv

@@ -525,6 +525,11 @@ project_query_kernel(const float* __restrict__ q, const float* __restrict__ w_k,
 
 cudaError_t launch_project_query(const float* q, const float* w_k, float* q_lat, int B, int Hq,
                                  int KV, int D, int L, cudaStream_t st) {
+    // The batched GEMM (4 x 4 outputs per thread, 16-byte operand loads)
+    // where the shapes allow it: 1024 query rows per KV head x 256 latent
+    // columns took 48 us per call in the 4 x 2 tiles below.
+    if (rows_gemm_supported(q, w_k, q_lat, D, L))
+        return launch_rows_gemm(q, w_k, true, q_lat, B, Hq, KV, D, L, st);
     const int M = B * (Hq / KV);
     dim3 grid((M + kPqRows - 1) / kPqRows, (L + kPqCols - 1) / kPqCols, KV);
     project_query_kernel<<<grid, 256, 0, st>>>(q, w_k, q_lat, B, Hq, KV, D, L);

@@ -217,3 +217,33 @@ def test_gqa_latent_tensor_core_pass_vs_oracle(ops, L, Hq, bs, target):
                                               w_v_canonical=c["w_v"], proj_heads=KV,
                                               head_dim=D, acc64=True, want_intermediates=False)
         assert rel_err(ctx[b], ec) <= EXACT_REL, (L, b, rel_err(ctx[b], ec))
+
+
+def test_gqa_projections_batched_gemm_vs_oracle(ops):
+    """40 sequences x 4 query heads per KV head = 160 rows per head: both the
+    query projection (W_k) and the value projection (W_v) run as the batched
+    FP32 GEMM (64 x 64 tiles, partial edge tiles: 160 rows, 128 / 256
+    columns). Query rows and contexts equal the FP64 restatement at 1e-5."""
+    rng = np.random.default_rng(91)
+    lens = list(rng.integers(1, 300, 40))
+    c = _gqa_case(91, lens, 256, 256)
+    KV, D = c["KV"], c["D"]
+    q_lat = ops.project_query(t(c["q"]), _head_major(c["w_k"], KV, D))
+    plan = ops.plan_splits(c["lens"], c["bs"], target_items=64)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    r = ops.latent_decode(q_lat, t(c["cache"]), t(c["tables"]), t(c["lens"]), plan,
+                          scale=1 / math.sqrt(D), value_dim=256,
+                          w_v=_head_major(c["w_v"], KV, D), flags=flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
+    ql_gpu = q_lat.cpu().numpy()
+    ctx = r["ctx"].cpu().numpy()
+    bits = c["cache"].view(np.uint16)
+    for b, n in enumerate(c["lens"]):
+        ql = c_ref.project_query(c["q"][b], c["w_k"], KV)
+        assert rel_err(ql_gpu[b], ql) <= EXACT_REL
+        _, _, _, ec = c_ref.latent_decode_seq(ql, bits, c["tables"][b], int(n), int(n), c["bs"],
+                                              1 / math.sqrt(D), value_dim=256,
+                                              w_v_canonical=c["w_v"], proj_heads=KV,
+                                              head_dim=D, acc64=True, want_intermediates=False)
+        assert rel_err(ctx[b], ec) <= EXACT_REL, (b, rel_err(ctx[b], ec))
