@@ -92,6 +92,25 @@ project_rows_kernel(const float* __restrict__ rows, void* const* __restrict__ ro
     const int p = blockIdx.x, d0 = blockIdx.y * 32, r0 = blockIdx.z * 8;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nrows = min(8, B * group - r0);
+    const float* wp = w + (int64_t)p * width * D;
+    const bool vec = (D & 3) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+    const uint64_t keep = l2_evict_last_policy();
+    const int lsub = lane >> 3, dq = lane & 7;
+    const int slice = warp * 4 + lsub;
+    const int dcol = d0 + 4 * dq;
+    // The first 8 weight rows of this thread do not depend on the rows:
+    // their loads are issued before the rows are staged, so that the two
+    // latencies overlap.
+    float4 wv[8];
+    if (vec && dcol < D) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int l = slice + 32 * u;
+            wv[u] = l < width ? ldg_f4_keep(reinterpret_cast<const float4*>(
+                                                wp + (int64_t)l * D + dcol), keep)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
     if ((width & 3) == 0) {
         const int w4 = width >> 2;
         for (int r = 0; r < 8; ++r) {
@@ -114,13 +133,7 @@ project_rows_kernel(const float* __restrict__ rows, void* const* __restrict__ ro
         }
     }
     __syncthreads();
-    const float* wp = w + (int64_t)p * width * D;
-    const bool vec = (D & 3) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
     if (vec) {
-        const uint64_t keep = l2_evict_last_policy();
-        const int lsub = lane >> 3, dq = lane & 7;
-        const int slice = warp * 4 + lsub;
-        const int dcol = d0 + 4 * dq;
         float acc[8][4];
 #pragma unroll
         for (int r = 0; r < 8; ++r)
@@ -128,13 +141,14 @@ project_rows_kernel(const float* __restrict__ rows, void* const* __restrict__ ro
             for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
         if (dcol < D) {
             for (int l0 = slice; l0 < width; l0 += 32 * 8) {
-                float4 wv[8];
+                if (l0 != slice) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int l = l0 + 32 * u;
-                    wv[u] = l < width ? ldg_f4_keep(reinterpret_cast<const float4*>(
-                                                        wp + (int64_t)l * D + dcol), keep)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int u = 0; u < 8; ++u) {
+                        const int l = l0 + 32 * u;
+                        wv[u] = l < width ? ldg_f4_keep(reinterpret_cast<const float4*>(
+                                                            wp + (int64_t)l * D + dcol), keep)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
                 }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
